@@ -1,0 +1,301 @@
+#!/usr/bin/env python
+"""Benchmark of the fused token sampler (one JSON line on rank 0).
+
+Workload (configs[1] of the baseline): B=128 rows, V=151936, fp16 logits
+N(0, 2.5^2) with 3% of ids per row shifted +6, four row groups (greedy,
+top-k only, top-p only, temperature + top-k + top-p); seeded synthetic data.
+A step is one sampler launch over the whole batch.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+native: K launches timed with CUDA events on the launching stream, inputs
+rotating through 8 device copies (311 MB > 126 MB L2) so every launch reads
+its logits from HBM.  ``e2e`` repeats the step through the public API with
+the logits in pinned host memory: H2D copy, launch, D2H of the ids.
+reference: the reference's CPU sampling path (torch port, all host threads).
+Under torchrun each rank samples its own batch (batch-sharded, no collective);
+time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused-sampler rows/sec & HBM GB/s at B=128,V=151936 fp16; µs/decode-step"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic(workload):
+    """DRAM bytes per launch from the committed ncu capture summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(workload)
+    return None
+
+
+class ClockSampler:
+    """Polls SM clock and clock-event reasons through NVML while running."""
+
+    def __init__(self, index: int, period: float = 0.002):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+            return self
+        names = {
+            "hw_slowdown": getattr(self._nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(self._nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(self._nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(self._nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake": getattr(self._nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                    mask = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    for k, bit in names.items():
+                        if mask & bit:
+                            self.reasons.add(k)
+                except Exception:
+                    pass
+                time.sleep(self.period)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_reference_rows_per_sec(w, target_s: float = 0.5, max_rows=None):
+    """Time the torch-CPU port of the reference path on a bounded sample."""
+    from oracle.torch_port import sample_batch_torch
+    threads = torch.get_num_threads()
+    rows = 8
+    args = lambda n: (w.logits[:n], w.temperature[:n], w.top_k[:n], w.top_p[:n], w.uniforms[:n])
+    t0 = time.perf_counter()
+    sample_batch_torch(*args(rows))
+    dt = time.perf_counter() - t0
+    rows = max(1, min(w.batch if max_rows is None else max_rows, int(rows * target_s / max(dt, 1e-3))))
+    return rows, threads, lambda: sample_batch_torch(*args(rows))
+
+
+def run_reference(a):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from ecahlang_b200 import workloads as W
+    w = W.config2(seed=0)
+    rows, threads, step = cpu_reference_rows_per_sec(w, target_s=0.25)
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = time.perf_counter() - t0
+    rps = rows * a.steps / dt
+    sample = f"{rows} of the 128 rows per step (rows 0..{rows - 1}), all four row groups interleaved by row index"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * dt / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": "c2_mixed B=128 V=151936 fp16 (bounded row sample per step)",
+                   "batch": 128, "vocab": 151936, "parallelism": "cpu"},
+        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": rps, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_native(a):
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
+                                             device_id=dev)
+    from ecahlang_b200 import sampler as S
+    from ecahlang_b200 import workloads as W
+
+    w = W.config2(seed=rank)
+    B, V = w.batch, w.vocab
+    bytes_in = w.logits.numel() * w.logits.element_size()
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits.to(dev) for _ in range(nbuf)]
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    smp = S.Sampler(B, V, w.logits.dtype, dev, seed=1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        smp(bufs[i % nbuf], T, K, P)
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(a.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.barrier()
+        ms = float(t.item())
+    torch.cuda.synchronize()
+    ms_step = ms / a.steps
+    rows_total = B * ws * a.steps
+    value = rows_total / (ms / 1e3)
+
+    # ---- e2e through the public API: pinned host logits -> device -> sample -> ids on host
+    host = w.logits.pin_memory()
+    hparams = [t.pin_memory() for t in (w.temperature, w.top_k, w.top_p)]
+    dlog = torch.empty_like(bufs[0])
+    dparams = [torch.empty_like(t, device=dev) for t in hparams]
+    ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    ke = max(3, min(a.steps, 50))
+
+    def e2e_step():
+        dlog.copy_(host, non_blocking=True)
+        for d, h in zip(dparams, hparams):
+            d.copy_(h, non_blocking=True)
+        out = smp(dlog, *dparams)
+        ids_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(ke):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ems], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = B * ws * ke / (ems / 1e3)
+    h2d = bytes_in + sum(t.numel() * t.element_size() for t in hparams)
+
+    line = None
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        alg = w.algorithmic_bytes() + B * (4 + 4 + 4 + 4)   # logits + T/k/p + ids
+        achieved = alg / (ms_step / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": ws, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms_step, "us_per_step": 1e3 * ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": "c2_mixed B=128 V=151936 fp16 (configs[1])", "batch_per_gpu": B,
+                       "vocab": V, "l2": f"inputs rotate through {nbuf} device copies "
+                       f"({nbuf * bytes_in / 2**20:.0f} MiB > 126 MiB L2)",
+                       "parallelism": f"batch-sharded x{ws}" if ws > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
+            "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke},
+            "gpu_launches": a.steps,
+            "clocks": clk.summary(),
+        }
+        if ws == 1 and not a.no_cpu_baseline:
+            rows, threads, cstep = cpu_reference_rows_per_sec(w, target_s=2.0)
+            cstep()
+            t0 = time.perf_counter()
+            n = 0
+            while time.perf_counter() - t0 < 10.0:
+                cstep()
+                n += 1
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {
+                "value": rows * n / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+                "sample": f"rows 0..{rows - 1} of the workload, {n} repetitions in {dt:.1f} s "
+                          f"(torch CPU port of the reference path, {threads} threads)"}
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_native(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+/*
+ * ecah_sampler.h -- C ABI of the B200 token sampler (libecah_sampler.so).
+ *
+ * The library replaces the per-step sampling expression of the ecahLang
+ * decode loop:
+ *
+ *   logits = logits / mask_penalty                      ecahlang/main.py:169
+ *   logits = logits / temperature                       ecahlang/main.py:170
+ *   idx = flashinfer.sampling.top_k_top_p_sampling_from_logits(
+ *             logits, top_k=..., top_p=..., deterministic=True)
+ *                                                       ecahlang/main.py:377-379
+ *   (same expression at main.py:398-402, :486-491, :579-584)
+ *
+ * and the per-token repetition-penalty table update
+ *
+ *   manager.mask_penalty[slot, idx] /= rp  (or *= rp)   ecahlang/main.py:691-694
+ *                                                       (also :519-522, :596-597)
+ *
+ * Every entry point takes plain device pointers and sizes, allocates nothing,
+ * never synchronises the host and never traps; all work is enqueued on the
+ * caller's stream, so the calls can be captured into a CUDA graph.  `stream`
+ * is a cudaStream_t passed as void* so this header needs no CUDA include.
+ * Status codes are returned; ecah_status_string() names them.
+ */
+#ifndef ECAH_SAMPLER_H
+#define ECAH_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ECAH_SAMPLER_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define ECAH_API __attribute__((visibility("default")))
+#else
+#define ECAH_API
+#endif
+
+/* logits dtype: the model dtype of ecahlang/env.py (--torch_dtype) */
+enum ecah_dtype { ECAH_DTYPE_F16 = 0, ECAH_DTYPE_BF16 = 1, ECAH_DTYPE_F32 = 2 };
+
+enum ecah_status {
+  ECAH_OK = 0,
+  ECAH_ERR_NULL = 1,       /* a required pointer is NULL                         */
+  ECAH_ERR_DTYPE = 2,      /* dtype is not one of enum ecah_dtype                */
+  ECAH_ERR_SHAPE = 3,      /* batch/vocab/stride out of range (vocab too large)  */
+  ECAH_ERR_WORKSPACE = 4,  /* workspace NULL or smaller than _workspace_bytes()  */
+  ECAH_ERR_LAUNCH = 5,     /* the CUDA launch itself failed                      */
+  ECAH_ERR_ABI = 6         /* args.abi_version does not match this library       */
+};
+
+/* flags */
+#define ECAH_FLAG_FREQ_PRES 0x1u /* apply frequency/presence penalties (additive) */
+
+/*
+ * One sampler launch.  Row r of the batch samples one token id from
+ * logits[r * row_stride + 0 .. vocab).  Per-row parameter arrays have `batch`
+ * entries (stride 1).  Semantics per row (the reference's op order):
+ *
+ *   y  = D(x / m(c))              repetition penalty, D = model dtype rounding,
+ *                                 m(c) = mask value after c updates (hist_mval),
+ *                                 m(c+1) = D(m(c) * rep_factor)
+ *   y' = y - (f*c + pi) [c > 0]   only with ECAH_FLAG_FREQ_PRES (not in the reference)
+ *   z  = y' / T                   float32; T <= 0 -> argmax (lowest index)
+ *   top-k (k <= 0 or k >= vocab: off), ties with the k-th value kept
+ *   softmax over the kept set, then top-p over it (p <= 0 or p >= 1: off)
+ *   draw: smallest index whose inclusive cumulative mass (vocab order) > u * Z
+ */
+typedef struct ecah_sampler_args {
+  int32_t abi_version;        /* = ECAH_SAMPLER_ABI_VERSION                      */
+  int32_t dtype;              /* enum ecah_dtype                                  */
+  int32_t batch;              /* B >= 0                                           */
+  int32_t vocab;              /* V >= 1                                           */
+  int64_t row_stride;         /* elements between rows, >= vocab                  */
+  const void* logits;         /* [B, row_stride] model dtype                      */
+  const float* temperature;   /* [B] (the reference's [B,1] buffer, contiguous)   */
+  const int32_t* top_k;       /* [B]                                              */
+  const float* top_p;         /* [B]                                              */
+  /* penalties: NULL pointers mean "none" */
+  const float* rep_factor;    /* [B] per-update mask multiplier: float32(1/rp) with the
+                                 reciprocal taken in double if rp > 1, else float32(rp)
+                                 -- what torch multiplies by for the reference's
+                                 `mask /= rp` / `mask *= rp` on a CUDA tensor.  Used only
+                                 to derive m(c) when hist_mval == NULL. */
+  const float* freq_pen;      /* [B] f  (ECAH_FLAG_FREQ_PRES)                      */
+  const float* pres_pen;      /* [B] pi (ECAH_FLAG_FREQ_PRES)                      */
+  /* per-slot token histories (the sparse form of mask_penalty[slot, :]) */
+  const int32_t* row_slot;    /* [B] slot of each row, -1 = no history; NULL = none */
+  const int32_t* slot_len;    /* [S] live entries per slot                         */
+  const int32_t* hist_tok;    /* [S, hist_cap] token ids (unique within a slot)    */
+  const int32_t* hist_cnt;    /* [S, hist_cap] counts                              */
+  const float* hist_mval;     /* [S, hist_cap] mask value m(c) in the model dtype,
+                                 or NULL to derive it from rep_factor and the count */
+  int32_t hist_cap;           /* entries per slot                                  */
+  int32_t num_slots;          /* S; rows whose slot is outside [0, S) have no history */
+  uint32_t flags;             /* ECAH_FLAG_*                                       */
+  /* randomness: uniforms[B] in [0,1) if given, else Philox4x32-10 with
+     state = {seed, offset}; the offset is advanced by 1 on the device after
+     the launch (CUDA-graph safe). */
+  const float* uniforms;
+  uint64_t* philox_state;     /* [2] device memory                                 */
+  int32_t* out;               /* [B] sampled token ids                             */
+  /* optional outputs (NULL = skip; they cost an extra pass when requested) */
+  float* row_stats;           /* [B, 4]: {y' threshold of the top-k set, y' threshold
+                                 of the final set, M = max z, Z = kept mass}; the
+                                 kept sets are {i : y'_i >= threshold}            */
+  float* probs_out;           /* [B, vocab] renormalised probabilities of the final
+                                 set (0 elsewhere); greedy rows get a one-hot row */
+  void* workspace;            /* >= ecah_sampler_workspace_bytes(), zero-filled once
+                                 before first use; left zero-filled by every launch */
+  size_t workspace_bytes;
+} ecah_sampler_args;
+
+ECAH_API int ecah_sampler_abi_version(void);
+ECAH_API const char* ecah_status_string(int status);
+
+/* Workspace needed by ecah_sampler_launch for this shape.  New entry point:
+ * FlashInfer's sampling ops allocate their row-state buffers themselves
+ * (called from ecahlang/main.py:377-379); here the caller owns them. */
+ECAH_API size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype);
+
+/* Sample one token per row.  Replaces the two divides and
+ * flashinfer.sampling.top_k_top_p_sampling_from_logits at
+ * ecahlang/main.py:169-170, :377-379, :398-402, :486-491, :579-584. */
+ECAH_API int ecah_sampler_launch(const ecah_sampler_args* args, void* stream);
+
+/* Record the sampled ids in the slot histories: for each row with
+ * row_slot[r] in [0, num_slots), the entry of token ids[r] gets count += 1
+ * and m <- D(m * rep_factor[r]) (a new entry starts at m = 1, count = 0
+ * before the update; rep_factor as in ecah_sampler_args, NULL = 1).  Replaces the per-request
+ * `mask_penalty[slot, idx] /= rp` launches of ecahlang/main.py:691-694
+ * (also :519-522, :596-597); a full slot sets overflow[slot] = 1 and drops
+ * the token.  `overflow` may be NULL. */
+ECAH_API int ecah_hist_update(const int32_t* ids, int32_t batch, const int32_t* row_slot,
+                              const float* rep_factor, int32_t* slot_len, int32_t* hist_tok,
+                              int32_t* hist_cnt, float* hist_mval, int32_t hist_cap,
+                              int32_t num_slots, int32_t dtype, int32_t* overflow,
+                              void* stream);
+
+/* The per-row uniforms the sampler draws with when args.uniforms == NULL
+ * (same Philox mapping), written to out[B]; advance != 0 also bumps the
+ * offset.  Stands in for the torch-generator seed/offset read of
+ * FlashInfer's sampling ops (called from ecahlang/main.py:377-379). */
+ECAH_API int ecah_philox_uniforms(uint64_t* philox_state, int32_t batch, float* out,
+                         int32_t advance, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ECAH_SAMPLER_H */

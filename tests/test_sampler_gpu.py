@@ -1,0 +1,301 @@
+"""GPU parity of the CUDA sampler against the CPU oracle (oracle/), through the
+C ABI.  Greedy ids and top-k sets must be bit-exact; final (top-p) sets,
+probabilities (1e-5 relative) and sampled ids must match except for rows
+whose u or top-p tail mass lies within 1e-6 of a boundary, which are counted
+and must stay rare."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, golden_history, load_golden
+from gpu_util import BOUNDARY, compare, run_gpu, run_oracle
+from ecahlang_b200 import sampler as S
+from ecahlang_b200 import workloads as W
+from oracle import sampler_oracle as so
+from oracle.philox import row_uniforms
+
+pytestmark = pytest.mark.gpu
+
+TDT = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+
+
+def _golden_tensor(d):
+    x = torch.from_numpy(d["logits_f32"].copy())
+    return x.to(TDT[d["dtype"]])
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+@pytest.mark.parametrize("top_p", [1.0, 0.9, 0.5])
+def test_golden_fixtures(name, top_p):
+    """The reference-pinned fixtures (penalty table, temperatures, top-k with
+    ties) through the CUDA path, with and without top-p."""
+    d = load_golden(name)
+    x = _golden_tensor(d)
+    B, V = x.shape
+    hist = golden_history(d)
+    T, K = d["temperature"], d["top_k"]
+    P = np.full(B, top_p, np.float32)
+    U = row_uniforms(11, 3, B)
+    gpu = run_gpu(x, T, K, P, U, history=hist, probs=V <= 4096)
+    orc = run_oracle(x, T, K, P, U, history=hist)
+    nb = compare(x, T, K, P, U, gpu, orc, history=hist, probs=gpu[2])
+    assert nb <= max(1, B // 8)
+
+
+def test_config2_mixed_full_size():
+    w = W.config2(seed=0)
+    gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
+    orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
+    nb = compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc)
+    assert nb <= 2
+
+
+@pytest.mark.parametrize("use_mval", [True, False])
+def test_config3_penalised(use_mval):
+    """Zipf histories with repetition + frequency + presence penalties (32-bit
+    key path).  use_mval=False derives m(c) from the counts in the kernel."""
+    w = W.config3(seed=0, B=32)
+    rp = w.rep_pen.numpy()
+    hist = []
+    for r, (t, c) in enumerate(w.history):
+        if use_mval:
+            mv = np.array([so.penalty_divisor(int(ci), float(rp[r]), "f16") for ci in c], np.float32)
+            hist.append((t, c, mv))
+        else:
+            hist.append((t, c))
+    args = dict(history=hist, rp=rp, f=w.freq_pen.numpy(), pi=w.pres_pen.numpy(), freq_pres=True)
+    gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, use_mval=use_mval, probs=True, **args)
+    orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, **args)
+    nb = compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, probs=gpu[2], **args)
+    assert nb <= 1
+
+
+def test_config1_fp32():
+    w = W.config1(seed=0)
+    gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, probs=True)
+    orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
+    compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, probs=gpu[2])
+
+
+def test_config4_bf16_subset():
+    w = W.config4(seed=0, B=48)
+    gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, probs=True)
+    orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
+    compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, probs=gpu[2])
+
+
+@pytest.mark.parametrize("V", [1, 2, 7, 33, 1000, 4097, 20481, 65537])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_odd_vocab_sizes(V, dtype):
+    g = torch.Generator().manual_seed(V)
+    B = 12
+    x = (torch.randn(B, V, generator=g) * 2).to(dtype)
+    T = np.array([1e-5, 0.5, 1.0, 2.0, 0.0, 1.0] * 2, np.float32)
+    K = np.array([0, 1, 3, V, 5, V - 1, 2, V + 5, -1, 10, 1, 0], np.int32)
+    P = np.array([1.0, 0.9, 0.5, 0.99, 1.0, 0.3, 1.0, 0.0, 0.7, 1e-6, 0.999999, 0.95], np.float32)
+    U = row_uniforms(V, 0, B)
+    gpu = run_gpu(x, T, K, P, U, probs=True)
+    orc = run_oracle(x, T, K, P, U)
+    compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
+
+
+def test_unaligned_rows_use_scalar_loads():
+    g = torch.Generator().manual_seed(5)
+    B, V = 6, 3001
+    x = (torch.randn(B, V, generator=g) * 3).half()
+    T = np.ones(B, np.float32)
+    K = np.array([0, 10, 100, 0, 1, 50], np.int32)
+    P = np.array([0.9, 1.0, 0.8, 1.0, 1.0, 0.5], np.float32)
+    U = row_uniforms(1, 1, B)
+    gpu = run_gpu(x, T, K, P, U, row_stride=V + 3)
+    orc = run_oracle(x, T, K, P, U)
+    compare(x, T, K, P, U, gpu, orc)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_ties_and_flat_rows(dtype):
+    g = torch.Generator().manual_seed(9)
+    B, V = 16, 30000
+    x = torch.round(torch.randn(B, V, generator=g) * 4) / 2   # many exact ties
+    x[0] = 0.0                                               # all equal
+    x[1, :] = -float("inf")
+    x[1, 123] = 1.0                                          # one finite logit
+    x = x.to(dtype)
+    T = np.array([1.0, 1.0, 1e-5, 0.7, 1.0, 3.0, 1.0, 0.5] * 2, np.float32)
+    K = np.array([7, 0, 0, 5, 1, 40, 2, 100, 0, 3, 17, 0, 1000, 2, 9, 0], np.int32)
+    P = np.array([1.0, 0.5, 1.0, 0.9, 1.0, 0.6, 0.95, 1.0, 0.5, 1.0, 0.25, 0.75, 0.9, 1.0, 0.3, 0.999], np.float32)
+    U = row_uniforms(3, 0, B)
+    gpu = run_gpu(x, T, K, P, U, probs=True)
+    orc = run_oracle(x, T, K, P, U)
+    nb = compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
+    assert nb <= 2
+
+
+def test_many_rows_small_vocab():
+    g = torch.Generator().manual_seed(21)
+    B, V = 2000, 300
+    x = (torch.randn(B, V, generator=g) * 2).half()
+    rng = np.random.default_rng(0)
+    T = rng.uniform(0.3, 1.5, B).astype(np.float32)
+    K = rng.integers(0, 60, B).astype(np.int32)
+    P = rng.choice([1.0, 0.9, 0.6], B).astype(np.float32)
+    U = row_uniforms(4, 0, B)
+    gpu = run_gpu(x, T, K, P, U)
+    orc = run_oracle(x, T, K, P, U)
+    nb = compare(x, T, K, P, U, gpu, orc)
+    assert nb <= 4
+
+
+def test_philox_device_matches_cpu_twin_and_advances():
+    dev = torch.device("cuda")
+    st = S.new_philox_state(0xDEADBEEF12345, 77, dev)
+    out = torch.empty(1000, dtype=torch.float32, device=dev)
+    from ecahlang_b200._abi import lib
+    assert lib().ecah_philox_uniforms(st.data_ptr(), 1000, out.data_ptr(), 1,
+                                      torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    want = row_uniforms(0xDEADBEEF12345, 77, 1000)
+    assert np.array_equal(out.cpu().numpy(), want)
+    assert st.cpu().tolist() == [0xDEADBEEF12345, 78]
+
+
+def test_sampler_philox_path_and_offset_bump():
+    dev = torch.device("cuda")
+    w = W.config2(seed=1, B=64, V=5000)
+    smp = S.Sampler(64, 5000, torch.float16, dev, seed=1234)
+    xd = w.logits.to(dev)
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    got = []
+    for _ in range(3):
+        got.append(smp(xd, T, K, P).clone())
+    torch.cuda.synchronize()
+    assert smp.philox_state.cpu().tolist() == [1234, 3]
+    for off in range(3):
+        U = row_uniforms(1234, off, 64)
+        ids = S.launch(xd, T, K, P, torch.empty(64, dtype=torch.int32, device=dev),
+                       S.new_workspace(64, 5000, torch.float16, dev), uniforms=torch.from_numpy(U).to(dev))
+        assert torch.equal(ids, got[off])
+
+
+def test_cuda_graph_capture_and_replay():
+    dev = torch.device("cuda")
+    w = W.config2(seed=2, B=32, V=151936)
+    smp = S.Sampler(32, w.vocab, torch.float16, dev, seed=99)
+    xd = w.logits.to(dev)
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        smp(xd, T, K, P)      # warm-up (offset 0 -> 1)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = smp(xd, T, K, P)
+    outs = []
+    for _ in range(3):
+        g.replay()
+        outs.append(out.clone())
+    torch.cuda.synchronize()
+    assert smp.philox_state.cpu().tolist() == [99, 4]
+    for i, o in enumerate(outs):
+        U = torch.from_numpy(row_uniforms(99, 1 + i, 32)).to(dev)
+        ref = S.launch(xd, T, K, P, torch.empty(32, dtype=torch.int32, device=dev),
+                       S.new_workspace(32, w.vocab, torch.float16, dev), uniforms=U)
+        assert torch.equal(ref, o)
+    del g
+
+
+def test_custom_op_matches_launch():
+    dev = torch.device("cuda")
+    w = W.config2(seed=3, B=16, V=20000)
+    xd = w.logits.to(dev)
+    T, K, P, U = (t.to(dev) for t in (w.temperature, w.top_k, w.top_p, w.uniforms))
+    out = torch.empty(16, dtype=torch.int32, device=dev)
+    ws = S.new_workspace(16, 20000, torch.float16, dev)
+    torch.ops.ecah.sample(xd, T, K, P, U, None, None, None, None, None, None, None, None, None, 0, 0, out, ws)
+    ref = S.launch(xd, T, K, P, torch.empty_like(out), ws, uniforms=U)
+    assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_penalty_rule_matches_torch_cuda_divide(dtype):
+    """The oracle's per-update rule against the reference's update statement
+    run by torch on the GPU, over many rp values and up to 60 repeats."""
+    dev = torch.device("cuda")
+    rps = [1.01, 1.05, 1.1, 1.17, 1.2, 1.3, 1.5, 1.7, 2.0, 3.3, 0.5, 0.8, 0.9, 0.95, 0.99, 1.0]
+    mask = torch.ones(len(rps), dtype=dtype, device=dev)
+    dts = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
+    for c in range(1, 61):
+        for i, rp in enumerate(rps):
+            if rp > 1:
+                mask[i] /= rp
+            else:
+                mask[i] *= rp
+        got = mask.float().cpu().numpy()
+        for i, rp in enumerate(rps):
+            assert got[i] == so.penalty_divisor(c, rp, dts), (dts, rp, c, got[i])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_hist_update_matches_reference_rule(dtype):
+    """Device-side history update vs the oracle's iterated mask rule, and that
+    rule vs torch's own CUDA in-place divide (the reference's update statement,
+    ecahlang/main.py:691-694, run on the GPU)."""
+    dev = torch.device("cuda")
+    S_, cap = 4, 64
+    pen = S.PenaltyState(S_, cap, dtype, dev)
+    rng = np.random.default_rng(1)
+    rps = [1.1, 1.3, 0.9, 2.0]
+    seq = rng.integers(0, 20, (30, S_))
+    row_slot = torch.arange(S_, dtype=torch.int32, device=dev)
+    rp_t = torch.from_numpy(S.repetition_factor(rps)).to(dev)
+    mask = torch.ones(S_, 32, dtype=dtype, device=dev)
+    for step in range(seq.shape[0]):
+        ids = torch.from_numpy(seq[step].astype(np.int32)).to(dev)
+        pen.update(ids, row_slot, rp_t)
+        for s in range(S_):
+            t = int(seq[step, s])
+            if rps[s] > 1:
+                mask[s, t] /= rps[s]
+            else:
+                mask[s, t] *= rps[s]
+    torch.cuda.synchronize()
+    dts = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
+    for s in range(S_):
+        n = int(pen.slot_len[s])
+        toks = pen.tok[s, :n].cpu().numpy()
+        cnts = pen.cnt[s, :n].cpu().numpy()
+        mv = pen.mval[s, :n].cpu().numpy()
+        u, c = np.unique(seq[:, s], return_counts=True)
+        assert sorted(toks.tolist()) == u.tolist()
+        assert dict(zip(toks.tolist(), cnts.tolist())) == dict(zip(u.tolist(), c.tolist()))
+        for t, cnt, m in zip(toks, cnts, mv):
+            assert m == so.penalty_divisor(int(cnt), rps[s], dts)
+            assert m == mask[s, t].float().item(), (s, t, cnt, m, mask[s, t].item())
+
+
+def test_chi_square_one_million_draws():
+    """1e6 draws of one distribution (Philox offsets 0..999 x 1000 rows)
+    against the oracle's post-filter probabilities."""
+    dev = torch.device("cuda")
+    V, B, steps = 256, 1000, 1000
+    g = torch.Generator().manual_seed(77)
+    row = (torch.randn(V, generator=g) * 1.5).half()
+    x = row.repeat(B, 1).to(dev)
+    T = torch.full((B,), 0.8, device=dev)
+    K = torch.full((B,), 120, dtype=torch.int32, device=dev)
+    P = torch.full((B,), 0.9, device=dev)
+    smp = S.Sampler(B, V, torch.float16, dev, seed=5)
+    counts = torch.zeros(V, dtype=torch.int64, device=dev)
+    for _ in range(steps):
+        ids = smp(x, T, K, P)
+        counts += torch.bincount(ids.long(), minlength=V)
+    res = so.sample_row(row.float().numpy(), dtype="f16", temperature=0.8, top_k=120, top_p=0.9)
+    c = counts.cpu().numpy()
+    keep = res.probs > 0
+    assert c[~keep].sum() == 0
+    exp = res.probs[keep] * B * steps
+    chi2 = float(((c[keep] - exp) ** 2 / exp).sum())
+    dof = int(keep.sum()) - 1
+    assert chi2 < dof + 6 * np.sqrt(2 * dof), (chi2, dof)
