@@ -31,6 +31,7 @@ template <> struct DType<ECAH_DTYPE_F16> {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(r)));
   }
   static __device__ __forceinline__ float round(float f) { return __half2float(__float2half_rn(f)); }
+  static __device__ __forceinline__ float round_down(float f) { return __half2float(__float2half_rd(f)); }
   static __device__ __forceinline__ uint32_t to_raw(float f) { return __half_as_ushort(__float2half_rn(f)); }
 };
 
@@ -39,6 +40,7 @@ template <> struct DType<ECAH_DTYPE_BF16> {
   static constexpr int kVec = 8;
   static __device__ __forceinline__ float to_f32(uint32_t r) { return __uint_as_float(r << 16); }
   static __device__ __forceinline__ float round(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
+  static __device__ __forceinline__ float round_down(float f) { return __bfloat162float(__float2bfloat16_rd(f)); }
   static __device__ __forceinline__ uint32_t to_raw(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 };
 
@@ -47,6 +49,7 @@ template <> struct DType<ECAH_DTYPE_F32> {
   static constexpr int kVec = 4;
   static __device__ __forceinline__ float to_f32(uint32_t r) { return __uint_as_float(r); }
   static __device__ __forceinline__ float round(float f) { return f; }
+  static __device__ __forceinline__ float round_down(float f) { return f; }
   static __device__ __forceinline__ uint32_t to_raw(float f) { return __float_as_uint(f); }
 };
 

@@ -80,6 +80,7 @@ constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private
 constexpr int kNBL = 512;     // bins of deeper levels / the key window
 constexpr int kWin = 512;     // keys in the window below the row max
 constexpr int kMaxSeg = 256;  // warp segments per CTA
+constexpr int kMaxCLs = 16;   // CTAs per cluster, at most
 
 // digit layout: 16-bit keys 7|9, 32-bit keys 7|9|8|8 (high to low)
 template <int KB> struct Radix;
@@ -115,29 +116,48 @@ template <> struct KV<32> {
   static __device__ __forceinline__ uint32_t vmax(const uint4& q) { return max(max(q.x, q.y), max(q.z, q.w)); }
 };
 
-// Per-CTA values published to the cluster, double-buffered by phase parity:
-// a set written before barrier s is read by peers between barriers s and s+1
-// and rewritten only after barrier s+1.
+// Generic-path values published to the cluster, double-buffered by phase
+// parity: a set written before barrier s is read by peers between barriers s
+// and s+1 and rewritten only after barrier s+1.
 struct PubSet {
-  unsigned c[kNBL];             // counts (window / deeper levels)
-  float m[kNBL];                // exact float masses (window / sub-bins)
+  unsigned c[kNBL];             // counts of one radix level
+  float m[kNBL];                // exact float masses of one radix level
   unsigned long long l0[kNB0];  // level-0 histogram (counts or fixed-point masses)
   float s;                      // exact mass partial (S or "mass above")
 };
 
 struct Smem {
-  unsigned lp[kNB0 * 32];       // lane-private level-0 histogram, [bin][lane]
+  union {
+    unsigned lp[kNB0 * 32];     // lane-private level-0 histogram, [bin][lane]
+    struct {                    // merged data, after the first barrier
+      unsigned cnt[kWin];       // window counts, bin b = key kmax - b
+      float e[kWin];            // mass of one token of key kmax - b
+      float m[kWin];            // cnt * e
+      float l0[kNB0];           // level-0 masses (rescaled to M)
+      float e3[kNBL];           // pass 3: mass of one token of key (b0 << 9) | d
+    } g;
+    struct {                    // generic path
+      unsigned mc[kNBL];
+      float mm[kNBL];
+    } q;
+  } u;
+  // published to the cluster
+  unsigned win[kWin];           // local window counts, bin b = key lmax - b
+  unsigned long long l0[kNB0];  // local level-0 fixed-point masses, relative to mref
+  unsigned c3[kNBL];            // pass 3: counts of keys in bin b0, index key & 511
   PubSet set[2];
-  unsigned mc[kNBL];            // merged counts
-  float mm[kNBL];               // merged masses
-  float ml0[kNB0];              // merged level-0 histogram (as float)
+  unsigned lmax;                // CTA-local max key
+  float mref;                   // value(lmax) / T
+  float sref;                   // sum of exp(z - mref) over the chunk (dense rows)
+  float total;                  // kept mass of the CTA (relative to M)
+  int first_idx;                // argmax index (greedy)
+  // cluster-gathered scalars (local copies)
+  unsigned plmax[kMaxCLs];
+  float pscale[kMaxCLs];        // exp(mref_c - M)
   float seg[kMaxSeg];           // kept mass per warp segment (draw)
   float red[kThreads / 32];
-  unsigned kmax;                // published row-max key
-  int first_idx;                // published argmax index (greedy)
-  float total;                  // published kept mass of the CTA
-  int ib[4];
-  float fb[4];
+  int ib[8];
+  float fb[8];
 };
 
 // Smallest key k in [0, hi] whose quotient value(k)/T reaches zthr.  The
@@ -320,6 +340,17 @@ __device__ __forceinline__ void cp_async_wait_all() {
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// Lower bound key below which every token has softmax mass exactly 0 relative
+// to m: y < (m - 100 - |m| 2^-20) T gives y/T - m < -99.9 even after the
+// roundings of the divide, and ex2 of less than -144 flushes to zero.
+template <int DT, int KB>
+__device__ __forceinline__ uint32_t zero_mass_cut(float m, float T) {
+  const float yc = __fmul_rn(__fsub_rn(__fsub_rn(m, 100.0f), __fmul_rn(fabsf(m), 9.5367431640625e-07f)), T);
+  if (!(yc == yc)) return 0u;
+  if (KB == 16) return key16(DType<DT>::to_raw(DType<DT>::round_down(yc)));
+  return key32(yc);
+}
+
 template <int DT, int KB>
 __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   using Dt = DType<DT>;
@@ -330,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   constexpr int N = KV<KB>::N;                        // keys per 16-byte vector
   constexpr int VIN = Dt::kVec;                       // logits per 16-byte global load
   constexpr bool kRawInSmem = sizeof(Raw) == sizeof(Key);
-  constexpr int SEG = 32 * N;                         // keys per warp segment
+  constexpr int kSegPerLane = kMaxSeg / 32;
 
   extern __shared__ __align__(16) unsigned char dsm[];
   Key* keys = reinterpret_cast<Key*>(dsm);
@@ -346,7 +377,11 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   const int nvec = (n + N - 1) / N;
   const Raw* src = reinterpret_cast<const Raw*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
 
-  for (int i = tid; i < kNB0 * 32; i += kThreads) S.lp[i] = 0u;
+  for (int i = tid; i < kWin; i += kThreads) S.win[i] = 0u;
+  for (int i = tid; i < kNBL; i += kThreads) S.c3[i] = 0u;
+  for (int i = tid; i < kNB0; i += kThreads) S.l0[i] = 0ull;
+  if (tid == 0) S.sref = 0.f;
+  for (int i = tid; i < kNB0 * 32; i += kThreads) S.u.lp[i] = 0u;
   {
     unsigned* z = reinterpret_cast<unsigned*>(&S.set[0]);
     for (int i = tid; i < static_cast<int>(2 * sizeof(PubSet) / 4); i += kThreads) z[i] = 0u;
@@ -433,10 +468,29 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   }
   __syncthreads();
 
-  // ----------------------------------------------- pass 1: keys, row max
+  // ------------------------------------------ pass 1: keys, local row max
+  uint32_t lmax_all;
   {
     uint32_t tmax = 0u;
-    for (int v = tid; v < nvec; v += kThreads) {
+    int v = tid;
+    for (; v + kThreads < nvec; v += 2 * kThreads) {
+      uint4 q0 = kv4[v], q1 = kv4[v + kThreads];
+      if constexpr (kRawInSmem) {
+        if constexpr (KB == 16) {
+          q0.x = key16x2(q0.x); q0.y = key16x2(q0.y); q0.z = key16x2(q0.z); q0.w = key16x2(q0.w);
+          q1.x = key16x2(q1.x); q1.y = key16x2(q1.y); q1.z = key16x2(q1.z); q1.w = key16x2(q1.w);
+        } else {
+          q0.x = key32(__uint_as_float(q0.x)); q0.y = key32(__uint_as_float(q0.y));
+          q0.z = key32(__uint_as_float(q0.z)); q0.w = key32(__uint_as_float(q0.w));
+          q1.x = key32(__uint_as_float(q1.x)); q1.y = key32(__uint_as_float(q1.y));
+          q1.z = key32(__uint_as_float(q1.z)); q1.w = key32(__uint_as_float(q1.w));
+        }
+        kv4[v] = q0;
+        kv4[v + kThreads] = q1;
+      }
+      tmax = max(tmax, max(KV<KB>::vmax(q0), KV<KB>::vmax(q1)));
+    }
+    if (v < nvec) {
       uint4 q = kv4[v];
       if constexpr (kRawInSmem) {
         if constexpr (KB == 16) {
@@ -452,25 +506,93 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
     tmax = __reduce_max_sync(0xFFFFFFFFu, tmax);
     if (lane == 0) S.red[warp] = __uint_as_float(tmax);
     __syncthreads();
-    if (tid == 0) {
-      uint32_t m = 0u;
-      for (int w = 0; w < kThreads / 32; ++w) m = max(m, __float_as_uint(S.red[w]));
-      S.kmax = m;
+    uint32_t m = 0u;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) m = max(m, __float_as_uint(S.red[w]));
+    if (tid == 0) S.lmax = m;
+    lmax_all = m;  // every thread computed the same value
+  }
+  const uint32_t lmax = lmax_all;
+  __syncthreads();
+
+  // ------------------- pass 2 (before any exchange; 16-bit keys, T > 0)
+  // top-k rows: counts of the 512 keys below the local max.  Rows without
+  // top-k: softmax masses relative to the local max mref (exact sum, 128-bin
+  // fixed-point histogram) plus the same window counts.  Peers rescale by
+  // exp(mref - M) once the row max M is known.
+  // Decisions here use only this CTA's data; everything after the first
+  // barrier uses cluster-uniform values (kmax and merged histograms) so every
+  // CTA takes the same branches and barriers.
+  const float rT = __frcp_rn(T);
+  const bool local_ok = (KB == 16) && (T > 0.f) && lmax >= static_cast<uint32_t>(kWin);
+  float mref = 0.f;
+  if (local_ok) {
+    const uint32_t lo_w = lmax - (kWin - 1);
+    mref = __fdiv_rn(C::value(lmax), T);
+    if (topk) {
+      for (int v = tid; v < nvec; v += kThreads) {
+        const uint4 q = kv4[v];
+        if (KV<KB>::vmax(q) < lo_w) continue;
+        uint32_t k[N];
+        KV<KB>::unpack(q, k);
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+          if (k[j] >= lo_w) atomicAdd(&S.win[lmax - k[j]], 1u);
+      }
+    } else if (isfinite(mref)) {
+      const uint32_t cut = zero_mass_cut<DT, KB>(mref, T);
+      const float fxs = P.fx_scale;
+      float sacc = 0.f;
+      for (int v = tid; v < nvec; v += kThreads) {
+        const uint4 q = kv4[v];
+        const uint32_t vm = KV<KB>::vmax(q);
+        if (vm < cut) continue;
+        uint32_t k[N];
+        KV<KB>::unpack(q, k);
+        float e[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) e[j] = (k[j] >= cut) ? mass_of(C::value(k[j]), T, rT, mref) : 0.f;
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          sacc += e[j];
+          atomicAdd(&S.u.lp[((k[j] >> 9) << 5) | lane], to_fixed(e[j], fxs));
+        }
+        if (vm >= lo_w) {
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+            if (k[j] >= lo_w) atomicAdd(&S.win[lmax - k[j]], 1u);
+        }
+      }
+      const float sb = block_sum(sacc, S.red);
+      __syncthreads();
+      if (tid < kNB0) {
+        unsigned long long acc = 0ull;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) acc += S.u.lp[(tid << 5) | ((j + tid) & 31)];
+        S.l0[tid] = acc;
+      }
+      if (tid == 0) S.sref = sb;
     }
   }
+  if (tid == 0) S.mref = mref;
+
   cluster.sync();  // ---------------------------------------------------- B1
   if (warp == 0) {
-    uint32_t km = (lane < P.CL) ? cluster.map_shared_rank(&S, lane)->kmax : 0u;
-    km = __reduce_max_sync(0xFFFFFFFFu, km);
-    if (lane == 0) S.ib[3] = static_cast<int>(km);
+    const uint32_t lm = (lane < P.CL) ? cluster.map_shared_rank(&S, lane)->lmax : 0u;
+    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, lm);
+    if (lane < kMaxCLs) S.plmax[lane] = lm;
+    if (lane == 0) S.ib[7] = static_cast<int>(km);
   }
   __syncthreads();
-  const uint32_t kmax = static_cast<uint32_t>(S.ib[3]);
-  int ps = 0;  // parity of the next published set
+  const uint32_t kmax = static_cast<uint32_t>(S.ib[7]);
+  int ps = 0;  // parity of the next published set (generic path)
 
   const float ymax = C::value(kmax);
   const float M = __fdiv_rn(ymax, T);
   const bool greedy = !(T > 0.f) || !isfinite(M);
+  // cluster-uniform path flags (finite rows have kmax >= key(-inf) > kWin)
+  const bool row_fast = (KB == 16) && (T > 0.f) && kmax >= static_cast<uint32_t>(kWin);
+  const bool dense = row_fast && !topk;
   int result = -1;
 
   if (greedy) {
@@ -515,200 +637,186 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
       for (int i = tid; i < n; i += kThreads) po[i] = (i == g) ? 1.0f : 0.0f;
     }
   } else {
-    const float rT = __frcp_rn(T);
-    const uint32_t key_cut = key_lower_bound<DT, KB>(__fsub_rn(M, kExpCut), T, kmax);
+    const uint32_t key_cut = zero_mass_cut<DT, KB>(M, T);
     uint32_t key_lo_k = 0u;   // top-k set: key >= key_lo_k
     uint32_t key_lo = 0u;     // final set: key >= key_lo
-    bool generic = (KB == 32);
-    bool need_topk = topk, need_topp = topp;
+    // how the CTA kept masses are obtained: 0 window counts, 1 dense sum,
+    // 2 level-0 + pass-3 counts, 3 full draw pass
+    int tmode = 3;
+    uint32_t b0 = 0u;
+    bool generic = !row_fast;
+    bool topk_done = false;
+    const bool have_local = local_ok && (lmax + static_cast<uint32_t>(kWin) > kmax);
 
-    // ------------------------------------------- 16-bit keys: window pass
-    if (KB == 16 && (topk || topp)) {
-      const uint32_t lo_w = kmax >= static_cast<uint32_t>(kWin - 1) ? kmax - (kWin - 1) : 0u;
-      PubSet& W = S.set[ps & 1];
-      const uint32_t skip_below = (topp && !topk) ? min(lo_w, key_cut) : lo_w;
-      float s_exact = 0.f;
-      const float fxs = P.fx_scale;
-      // padding keys are 0, below lo_w and key_cut: no bounds checks needed
-      auto win_key = [&](uint32_t kj) {
-        if (topk && kj >= lo_w) atomicAdd(&W.c[kmax - kj], 1u);
-        if (topp && kj >= key_cut && (kj >= lo_w || !topk)) {
-          const float e = mass_of(C::value(kj), T, rT, M);
-          if (kj >= lo_w) atomicAdd(&W.m[kmax - kj], e);
-          if (!topk) {
-            s_exact += e;
-            atomicAdd(&S.lp[((kj >> 9) << 5) | lane], to_fixed(e, fxs));
-          }
+    if (row_fast) {
+      // ---------------------------------------------- merge the window
+      if (warp == 0) {
+        float sc = 0.f;
+        if (lane < P.CL) {
+          const float mr = cluster.map_shared_rank(&S, lane)->mref;
+          sc = dense ? ex2_approx(__fmul_rn(__fsub_rn(mr, M), kLog2e)) : 0.f;
         }
-      };
-      int v = tid;
-      for (; v + kThreads < nvec; v += 2 * kThreads) {
-        const uint4 q0 = kv4[v], q1 = kv4[v + kThreads];
-        const bool a0 = KV<KB>::vmax(q0) >= skip_below, a1 = KV<KB>::vmax(q1) >= skip_below;
-        if (a0) {
-          uint32_t k[N];
-          KV<KB>::unpack(q0, k);
-#pragma unroll
-          for (int j = 0; j < N; ++j) win_key(k[j]);
-        }
-        if (a1) {
-          uint32_t k[N];
-          KV<KB>::unpack(q1, k);
-#pragma unroll
-          for (int j = 0; j < N; ++j) win_key(k[j]);
-        }
-      }
-      if (v < nvec) {
-        const uint4 q0 = kv4[v];
-        if (KV<KB>::vmax(q0) >= skip_below) {
-          uint32_t k[N];
-          KV<KB>::unpack(q0, k);
-#pragma unroll
-          for (int j = 0; j < N; ++j) win_key(k[j]);
-        }
-      }
-      if (topp && !topk) {
-        const float s_blk = block_sum(s_exact, S.red);
-        __syncthreads();
-        if (tid < kNB0) {
-          unsigned long long acc = 0ull;
-#pragma unroll 8
-          for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
-          W.l0[tid] = acc;
-        }
-        if (tid == 0) W.s = s_blk;
-        __syncthreads();
-        for (int i = tid; i < kNB0 * 32; i += kThreads) S.lp[i] = 0u;
-      }
-      cluster.sync();  // ------------------------------------------------ B2
-      // merge the window (and level-0 masses)
-      for (int b = tid; b < kWin; b += kThreads) {
-        S.mc[b] = topk ? cluster_sum(cluster, &S.set[ps & 1].c[b], P.CL) : 0u;
-        S.mm[b] = topp ? cluster_sum(cluster, &S.set[ps & 1].m[b], P.CL) : 0.f;
-      }
-      float S_all = 0.f;
-      if (topp && !topk) {
-        if (tid < kNB0)
-          S.ml0[tid] = static_cast<float>(cluster_sum(cluster, &S.set[ps & 1].l0[tid], P.CL)) * P.fx_inv;
-        S_all = cluster_sum(cluster, &S.set[ps & 1].s, P.CL);
-      }
-      ++ps;
-      {  // the next published set must start empty
-        unsigned* z = reinterpret_cast<unsigned*>(&S.set[ps & 1]);
-        for (int i = tid; i < static_cast<int>(sizeof(PubSet) / 4); i += kThreads) z[i] = 0u;
+        if (lane < kMaxCLs) S.pscale[lane] = sc;
       }
       __syncthreads();
+      for (int b = tid; b < kWin; b += kThreads) {
+        unsigned cs = 0u;
+        for (int base = 0; base < P.CL; base += 8) {
+          unsigned vv[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int r = base + j < P.CL ? base + j : base;
+            const int idx = b - static_cast<int>(kmax - S.plmax[r]);
+            vv[j] = *cluster.map_shared_rank(&S.win[idx >= 0 && idx < kWin ? idx : 0], r);
+            if (!(idx >= 0 && idx < kWin) || base + j >= P.CL) vv[j] = 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cs += vv[j];
+        }
+        const float e = (kmax >= static_cast<uint32_t>(b)) ? mass_of(C::value(kmax - b), T, rT, M) : 0.f;
+        S.u.g.cnt[b] = cs;
+        S.u.g.e[b] = e;
+        S.u.g.m[b] = __fmul_rn(static_cast<float>(cs), e);
+      }
+      float S_all = 0.f;
+      if (dense) {
+        if (tid < kNB0) {
+          float a = 0.f;
+          for (int r = 0; r < P.CL; ++r)
+            a += __fmul_rn(static_cast<float>(*cluster.map_shared_rank(&S.l0[tid], r)) * P.fx_inv, S.pscale[r]);
+          S.u.g.l0[tid] = a;
+        }
+        if (warp == 0) {
+          const float sr = (lane < P.CL) ? __fmul_rn(cluster.map_shared_rank(&S, lane)->sref, S.pscale[lane]) : 0.f;
+          float incl = sr;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          if (lane == 31) S.fb[5] = incl;
+        }
+      }
+      __syncthreads();
+      if (dense) S_all = S.fb[5];
 
-      bool have_p = false;
+      // ------------------------------------------------------ top-k
       if (topk) {
         if (warp == 0) {
           unsigned tot = 0u;
 #pragma unroll
-          for (int j = 0; j < kWin / 32; ++j) tot += S.mc[lane * (kWin / 32) + j];
-          tot = __reduce_add_sync(0xFFFFFFFFu, tot);  // window holds >= k keys?
+          for (int j = 0; j < kWin / 32; ++j) tot += S.u.g.cnt[lane * (kWin / 32) + j];
+          tot = __reduce_add_sync(0xFFFFFFFFu, tot);
           int b; unsigned above;
-          warp_select<unsigned, kWin, false>(S.mc, static_cast<unsigned>(k_eff), &b, &above);
-          if (lane == 0) S.ib[0] = (tot >= static_cast<unsigned>(k_eff)) ? b : -1;
+          warp_select<unsigned, kWin, false>(S.u.g.cnt, static_cast<unsigned>(k_eff), &b, &above);
+          if (lane == 0) {
+            int bk = (tot >= static_cast<unsigned>(k_eff)) ? b : -1;
+            uint32_t klk = 0u;
+            if (bk >= 0) klk = tie_floor<DT, KB>(kmax - static_cast<uint32_t>(bk), T);
+            S.ib[0] = bk;
+            S.ib[1] = static_cast<int>(klk);
+          }
         }
         __syncthreads();
         const int bk = S.ib[0];
         if (bk >= 0) {
-          const uint32_t tau_k = kmax - static_cast<uint32_t>(bk);
-          key_lo_k = tie_floor<DT, KB>(tau_k, T);
-          need_topk = false;
-          if (topp && key_lo_k < lo_w) generic = true;  // K straddles the window
+          key_lo_k = static_cast<uint32_t>(S.ib[1]);
+          key_lo = key_lo_k;
+          topk_done = true;
+          if (key_lo_k + static_cast<uint32_t>(kWin - 1) >= kmax) tmode = 0;  // K inside the window
+          else if (topp) generic = true;
         } else {
-          generic = true;  // k larger than the window
+          generic = true;
         }
-        __syncthreads();
+      } else {
+        tmode = 1;
       }
+
+      // ------------------------------------------------------ top-p
       if (topp && !generic) {
-        // S_K and the top-p bin inside the window
         const int bmax = topk ? static_cast<int>(kmax - key_lo_k) : kWin - 1;
         for (int b = tid; b < kWin; b += kThreads)
-          if (b > bmax) S.mm[b] = 0.f;
+          if (b > bmax) S.u.g.m[b] = 0.f;  // outside the top-k set
         __syncthreads();
         if (warp == 0) {
           float s = 0.f;
 #pragma unroll
-          for (int j = 0; j < kWin / 32; ++j) s += S.mm[lane * (kWin / 32) + j];
+          for (int j = 0; j < kWin / 32; ++j) {
+            const int b = lane * (kWin / 32) + j;
+            s += (b <= bmax) ? S.u.g.m[b] : 0.f;
+          }
           s = warp_sum(s);
           const float S_K = topk ? s : S_all;
           const float target = __fmul_rn(pp, S_K);
           int b; float above;
-          warp_select<float, kWin, false>(S.mm, target, &b, &above);
+          warp_select<float, kWin, false>(S.u.g.m, target, &b, &above);
           if (lane == 0) {
-            S.ib[1] = (s >= target) ? b : -1;
+            const bool in_win = s >= target && b <= bmax;
+            S.ib[2] = in_win ? b : -1;
             S.fb[0] = target;
+            if (in_win) S.ib[3] = static_cast<int>(tie_floor<DT, KB>(kmax - static_cast<uint32_t>(b), T));
           }
         }
         __syncthreads();
-        const int bp = S.ib[1];
         const float target = S.fb[0];
-        if (bp >= 0) {
-          key_lo = tie_floor<DT, KB>(kmax - static_cast<uint32_t>(bp), T);
-          have_p = true;
+        if (S.ib[2] >= 0) {
+          key_lo = static_cast<uint32_t>(S.ib[3]);
+          tmode = (key_lo + static_cast<uint32_t>(kWin - 1) >= kmax) ? 0 : 3;
+        } else if (!dense) {
+          generic = true;
         } else {
-          // nucleus wider than the window: level-0 bin, then its 512 keys
+          // nucleus wider than the window: level-0 bin, then exact counts of
+          // the 512 keys of that bin
           if (warp == 0) {
             int b; float above;
-            warp_select<float, kNB0, true>(S.ml0, target, &b, &above);
-            if (lane == 0) S.ib[2] = b;
+            warp_select<float, kNB0, true>(S.u.g.l0, target, &b, &above);
+            if (lane == 0) { S.ib[4] = b; S.fb[1] = above; }
           }
           __syncthreads();
-          const uint32_t b0 = static_cast<uint32_t>(S.ib[2]);
-          PubSet& Q = S.set[ps & 1];
-          float above = 0.f;
-          const uint32_t lo = max(b0 << 9, key_cut);
+          b0 = static_cast<uint32_t>(S.ib[4]);
+          const float above_b0 = S.fb[1];
+          const uint32_t lo3 = b0 << 9, hi3 = lo3 | 511u;
           for (int v = tid; v < nvec; v += kThreads) {
             const uint4 q = kv4[v];
-            if (KV<KB>::vmax(q) < lo) continue;
+            if (KV<KB>::vmax(q) < lo3) continue;
             uint32_t k[N];
             KV<KB>::unpack(q, k);
 #pragma unroll
-            for (int j = 0; j < N; ++j) {
-              const uint32_t kj = k[j];
-              if (kj >= lo) {
-                const float e = mass_of(C::value(kj), T, rT, M);
-                if ((kj >> 9) == b0) atomicAdd(&Q.m[kj & 511u], e);
-                else above += e;
-              }
-            }
+            for (int j = 0; j < N; ++j)
+              if (k[j] >= lo3 && k[j] <= hi3) atomicAdd(&S.c3[k[j] & 511u], 1u);
           }
-          const float ab = block_sum(above, S.red);
-          if (tid == 0) Q.s = ab;
-          cluster.sync();  // ---------------------------------------------- B3
-          for (int b = tid; b < kNBL; b += kThreads) S.mm[b] = cluster_sum(cluster, &S.set[ps & 1].m[b], P.CL);
-          if (tid == 0) S.fb[1] = cluster_sum(cluster, &S.set[ps & 1].s, P.CL);
-          ++ps;
-          {
-            unsigned* z = reinterpret_cast<unsigned*>(&S.set[ps & 1]);
-            for (int i = tid; i < static_cast<int>(sizeof(PubSet) / 4); i += kThreads) z[i] = 0u;
-          }
+          for (int d = tid; d < kNBL; d += kThreads)
+            S.u.g.e3[d] = mass_of(C::value(lo3 | static_cast<uint32_t>(d)), T, rT, M);
+          cluster.sync();  // ---------------------------------------------- B2
+          float* mm = S.u.g.m;  // reuse: merged pass-3 masses per key
+          for (int d = tid; d < kNBL; d += kThreads)
+            mm[d] = __fmul_rn(static_cast<float>(cluster_sum(cluster, &S.c3[d], P.CL)), S.u.g.e3[d]);
           __syncthreads();
           if (warp == 0) {
-            int d; float ab2;
-            warp_select<float, kNBL, true>(S.mm, __fsub_rn(target, S.fb[1]), &d, &ab2);
-            if (lane == 0) S.ib[3] = d;
+            int d; float ab;
+            warp_select<float, kNBL, true>(mm, __fsub_rn(target, above_b0), &d, &ab);
+            if (lane == 0) S.ib[5] = static_cast<int>(tie_floor<DT, KB>(lo3 | static_cast<uint32_t>(d), T));
           }
           __syncthreads();
-          key_lo = tie_floor<DT, KB>((b0 << 9) | static_cast<uint32_t>(S.ib[3]), T);
-          have_p = true;
+          key_lo = static_cast<uint32_t>(S.ib[5]);
+          tmode = (key_lo >= lo3) ? 2 : 3;
         }
-        need_topp = false;
       }
-      if (!topp) key_lo = key_lo_k;
-      if (topp && have_p && topk) key_lo = max(key_lo, key_lo_k);
     }
 
     // ------------------------------------------------ generic radix path
     if (generic) {
-      if (need_topk) {
+      tmode = 3;
+      if (topk && !topk_done) {
         uint32_t prefix = 0u;
         unsigned krem = static_cast<unsigned>(k_eff);
         for (int lev = 0; lev < R::kLevels; ++lev) {
           const int sh = R::shift(lev), wd = R::width(lev);
           PubSet& Q = S.set[ps & 1];
+          if (lev == 0) {
+            for (int i = tid; i < kNB0 * 32; i += kThreads) S.u.lp[i] = 0u;
+            __syncthreads();
+          }
           for (int v = tid; v < nvec; v += kThreads) {
             const uint4 q = kv4[v];
             if (lev > 0 && KV<KB>::vmax(q) < (prefix << (sh + wd))) continue;
@@ -720,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
               if (j >= lim) break;
               const uint32_t kj = k[j];
               if (lev == 0) {
-                atomicAdd(&S.lp[((kj >> sh) << 5) | lane], 1u);
+                atomicAdd(&S.u.lp[((kj >> sh) << 5) | lane], 1u);
               } else if ((kj >> (sh + wd)) == prefix) {
                 atomicAdd(&Q.c[(kj >> sh) & ((1u << wd) - 1u)], 1u);
               }
@@ -731,17 +839,15 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
             if (tid < kNB0) {
               unsigned long long acc = 0ull;
 #pragma unroll 8
-              for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
+              for (int j = 0; j < 32; ++j) acc += S.u.lp[(tid << 5) | ((j + tid) & 31)];
               Q.l0[tid] = acc;
             }
-            __syncthreads();
-            for (int i = tid; i < kNB0 * 32; i += kThreads) S.lp[i] = 0u;
           }
           cluster.sync();
           const int nb = 1 << wd;
           for (int b = tid; b < nb; b += kThreads)
-            S.mc[b] = (lev == 0) ? static_cast<unsigned>(cluster_sum(cluster, &S.set[ps & 1].l0[b], P.CL))
-                                 : cluster_sum(cluster, &S.set[ps & 1].c[b], P.CL);
+            S.u.q.mc[b] = (lev == 0) ? static_cast<unsigned>(cluster_sum(cluster, &S.set[ps & 1].l0[b], P.CL))
+                                     : cluster_sum(cluster, &S.set[ps & 1].c[b], P.CL);
           ++ps;
           {
             unsigned* z = reinterpret_cast<unsigned*>(&S.set[ps & 1]);
@@ -750,9 +856,9 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
           __syncthreads();
           if (warp == 0) {
             int b; unsigned above;
-            if (nb == 128) warp_select<unsigned, 128, true>(S.mc, krem, &b, &above);
-            else if (nb == 256) warp_select<unsigned, 256, true>(S.mc, krem, &b, &above);
-            else warp_select<unsigned, 512, true>(S.mc, krem, &b, &above);
+            if (nb == 128) warp_select<unsigned, 128, true>(S.u.q.mc, krem, &b, &above);
+            else if (nb == 256) warp_select<unsigned, 256, true>(S.u.q.mc, krem, &b, &above);
+            else warp_select<unsigned, 512, true>(S.u.q.mc, krem, &b, &above);
             if (lane == 0) { S.ib[0] = b; S.ib[1] = static_cast<int>(above); }
           }
           __syncthreads();
@@ -772,6 +878,10 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
           PubSet& Q = S.set[ps & 1];
           float acc = 0.f;  // level 0: S_K partial; deeper: mass above the prefix range
           const float fxs = P.fx_scale;
+          if (lev == 0) {
+            for (int i = tid; i < kNB0 * 32; i += kThreads) S.u.lp[i] = 0u;
+            __syncthreads();
+          }
           const uint32_t lo_lev = (lev == 0) ? klo : max(klo, prefix << (sh + wd));
           for (int v = tid; v < nvec; v += kThreads) {
             const uint4 q = kv4[v];
@@ -785,7 +895,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
               if (lev == 0) {
                 const float e = mass_of(C::value(kj), T, rT, M);
                 acc += e;
-                atomicAdd(&S.lp[((kj >> sh) << 5) | lane], to_fixed(e, fxs));
+                atomicAdd(&S.u.lp[((kj >> sh) << 5) | lane], to_fixed(e, fxs));
               } else {
                 const uint32_t hi = kj >> (sh + wd);
                 if (hi < prefix) continue;
@@ -800,18 +910,16 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
             if (tid < kNB0) {
               unsigned long long a2 = 0ull;
 #pragma unroll 8
-              for (int j = 0; j < 32; ++j) a2 += S.lp[(tid << 5) | ((j + tid) & 31)];
+              for (int j = 0; j < 32; ++j) a2 += S.u.lp[(tid << 5) | ((j + tid) & 31)];
               Q.l0[tid] = a2;
             }
-            __syncthreads();
-            for (int i = tid; i < kNB0 * 32; i += kThreads) S.lp[i] = 0u;
           }
           if (tid == 0) Q.s = accb;
           cluster.sync();
           const int nb = 1 << wd;
           for (int b = tid; b < nb; b += kThreads)
-            S.mm[b] = (lev == 0) ? static_cast<float>(cluster_sum(cluster, &S.set[ps & 1].l0[b], P.CL)) * P.fx_inv
-                                 : cluster_sum(cluster, &S.set[ps & 1].m[b], P.CL);
+            S.u.q.mm[b] = (lev == 0) ? static_cast<float>(cluster_sum(cluster, &S.set[ps & 1].l0[b], P.CL)) * P.fx_inv
+                                     : cluster_sum(cluster, &S.set[ps & 1].m[b], P.CL);
           if (tid == 0) S.fb[2] = cluster_sum(cluster, &S.set[ps & 1].s, P.CL);
           ++ps;
           {
@@ -823,9 +931,9 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
           const float goal = (lev == 0) ? target : __fsub_rn(target, S.fb[2]);
           if (warp == 0) {
             int b; float above;
-            if (nb == 128) warp_select<float, 128, true>(S.mm, goal, &b, &above);
-            else if (nb == 256) warp_select<float, 256, true>(S.mm, goal, &b, &above);
-            else warp_select<float, 512, true>(S.mm, goal, &b, &above);
+            if (nb == 128) warp_select<float, 128, true>(S.u.q.mm, goal, &b, &above);
+            else if (nb == 256) warp_select<float, 256, true>(S.u.q.mm, goal, &b, &above);
+            else warp_select<float, 512, true>(S.u.q.mm, goal, &b, &above);
             if (lane == 0) S.ib[0] = b;
           }
           __syncthreads();
@@ -839,40 +947,72 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
     // ---------------------------------------------------------- draw
     const uint32_t kdraw = max(key_lo, key_cut);
     const int nseg = (nvec + 31) / 32;
-    // kept mass per warp segment (32 consecutive vectors); padding keys are 0
-    for (int s = warp; s < nseg; s += kThreads / 32) {
-      const int v = s * 32 + lane;
-      float acc = 0.f;
-      if (v < nvec) {
-        const uint4 q = kv4[v];
-        if (KV<KB>::vmax(q) >= kdraw) {
-          uint32_t k[N];
-          KV<KB>::unpack(q, k);
+    auto segment_pass = [&]() {
+      // kept mass per warp segment (32 consecutive vectors); padding keys are 0
+      for (int s = warp; s < nseg; s += kThreads / 32) {
+        const int v = s * 32 + lane;
+        float acc = 0.f;
+        if (v < nvec) {
+          const uint4 q = kv4[v];
+          if (KV<KB>::vmax(q) >= kdraw) {
+            uint32_t k[N];
+            KV<KB>::unpack(q, k);
 #pragma unroll
-          for (int j = 0; j < N; ++j)
-            if (k[j] >= kdraw) acc += mass_of(C::value(k[j]), T, rT, M);
+            for (int j = 0; j < N; ++j)
+              if (k[j] >= kdraw) acc += mass_of(C::value(k[j]), T, rT, M);
+          }
         }
+        if (__any_sync(0xFFFFFFFFu, acc > 0.f)) acc = warp_sum(acc);
+        if (lane == 0) S.seg[s] = acc;
       }
-      if (__any_sync(0xFFFFFFFFu, acc > 0.f)) acc = warp_sum(acc);
-      if (lane == 0) S.seg[s] = acc;
-    }
-    __syncthreads();
-    // CTA total: lanes own contiguous segment ranges, scanned in order
-    constexpr int kSegPerLane = kMaxSeg / 32;
-    if (warp == 0) {
+      __syncthreads();
+    };
+    auto segment_total = [&]() -> float {  // warp 0: lanes own contiguous segment ranges
       float sl = 0.f;
 #pragma unroll
       for (int j = 0; j < kSegPerLane; ++j) {
         const int s = lane * kSegPerLane + j;
         if (s < nseg) sl += S.seg[s];
       }
-      float incl = sl;
+      return sl;
+    };
+    // kept mass of this CTA
+    if (tmode == 3) {
+      segment_pass();
+      if (warp == 0) {
+        float incl = segment_total();
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (lane == 31) S.total = incl;
       }
-      if (lane == 31) S.total = incl;
+    } else if (tmode == 1) {
+      if (tid == 0) S.total = __fmul_rn(S.sref, S.pscale[rank]);
+    } else if (tmode == 0) {
+      // this CTA's window keys >= kdraw, at per-key masses of the merged window
+      float acc = 0.f;
+      if (have_local) {
+        const int dl = static_cast<int>(kmax - lmax);
+        for (int b = tid; b < kWin; b += kThreads) {
+          const uint32_t key = lmax - static_cast<uint32_t>(b);
+          const int gb = b + dl;
+          if (key >= kdraw && gb < kWin && S.win[b]) acc += __fmul_rn(static_cast<float>(S.win[b]), S.u.g.e[gb]);
+        }
+      }
+      const float t = block_sum(acc, S.red);
+      if (tid == 0) S.total = t;
+    } else {
+      // level-0 bins above b0 (fixed point) + this CTA's pass-3 keys >= key_lo
+      float acc = 0.f;
+      if (tid < kNB0 && static_cast<uint32_t>(tid) > b0)
+        acc = __fmul_rn(static_cast<float>(S.l0[tid]) * P.fx_inv, S.pscale[rank]);
+      for (int d = tid; d < kNBL; d += kThreads)
+        if (((b0 << 9) | static_cast<uint32_t>(d)) >= kdraw && S.c3[d])
+          acc += __fmul_rn(static_cast<float>(S.c3[d]), S.u.g.e3[d]);
+      const float t = block_sum(acc, S.red);
+      if (tid == 0) S.total = t;
     }
     cluster.sync();  // ------------------------------------------------ draw
     if (warp == 0) {
@@ -899,119 +1039,113 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
         S.ib[1] = take_last;
         S.fb[0] = __fsub_rn(target, run_sel);
         S.fb[1] = Z;
-      }
-    }
-    if (tid == 0) {
-      const float Z = S.fb[1];
-      if (P.row_stats && rank == 0) {
-        float* st = P.row_stats + 4ll * row;
-        st[0] = topk ? C::value(key_lo_k) : -INFINITY;
-        st[1] = (topk || topp) ? C::value(key_lo) : -INFINITY;
-        st[2] = M;
-        st[3] = Z;
+        if (P.row_stats && rank == 0) {
+          float* st = P.row_stats + 4ll * row;
+          st[0] = topk ? C::value(key_lo_k) : -INFINITY;
+          st[1] = (topk || topp) ? C::value(key_lo) : -INFINITY;
+          st[2] = M;
+          st[3] = Z;
+        }
       }
     }
     __syncthreads();
-    cluster_arrive();  // peers may still read S.total until the final wait
+    cluster_arrive();  // peers may still read this CTA's shared memory until the final wait
     const int rsel = S.ib[0];
-    if (rsel == rank && warp == 0) {
-      const bool take_last = S.ib[1] != 0;
-      const float rem = S.fb[0];
-      // segment: lane ranges, then sequential within the lane
-      float sl = 0.f;
+    if (rsel == rank) {
+      if (tmode != 3) segment_pass();
+      if (warp == 0) {
+        const bool take_last = S.ib[1] != 0;
+        const float rem = S.fb[0];
+        // segment: lane ranges, then sequential within the lane
+        const float sl = segment_total();
+        float incl = sl;
 #pragma unroll
-      for (int j = 0; j < kSegPerLane; ++j) {
-        const int s = lane * kSegPerLane + j;
-        if (s < nseg) sl += S.seg[s];
-      }
-      float incl = sl;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-      if (lane == 0) excl = 0.f;
-      unsigned hit = take_last ? 0u : __ballot_sync(0xFFFFFFFFu, sl > 0.f && incl > rem);
-      bool last = take_last;
-      int L;
-      if (hit) {
-        L = __ffs(hit) - 1;
-      } else {
-        const unsigned nz = __ballot_sync(0xFFFFFFFFu, sl > 0.f);
-        L = nz ? 31 - __clz(nz) : 0;
-        last = true;
-      }
-      int sel = -1;
-      float rem2 = 0.f;
-      if (lane == L) {
-        float run = excl;
-        int slast = -1;
-        for (int j = 0; j < kSegPerLane; ++j) {
-          const int s = lane * kSegPerLane + j;
-          if (s >= nseg) break;
-          const float vs = S.seg[s];
-          if (vs > 0.f) slast = s;
-          if (!last && sel < 0 && vs > 0.f && run + vs > rem) { sel = s; rem2 = __fsub_rn(rem, run); }
-          run += vs;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
         }
-        if (sel < 0) { sel = slast; last = true; }
-        if (sel < 0) sel = 0;
-      }
-      sel = __shfl_sync(0xFFFFFFFFu, sel, L);
-      rem2 = __shfl_sync(0xFFFFFFFFu, rem2, L);
-      last = __shfl_sync(0xFFFFFFFFu, last, L);
-      // within the segment: one vector per lane
-      const int v = sel * 32 + lane;
-      float ev[N];
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < N; ++j) ev[j] = 0.f;
-      if (v < nvec) {
-        const uint4 q = kv4[v];
-        uint32_t k[N];
-        KV<KB>::unpack(q, k);
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          if (k[j] >= kdraw) ev[j] = mass_of(C::value(k[j]), T, rT, M);
-          acc += ev[j];
+        float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+        if (lane == 0) excl = 0.f;
+        const unsigned hit = take_last ? 0u : __ballot_sync(0xFFFFFFFFu, sl > 0.f && incl > rem);
+        bool last = take_last;
+        int L;
+        if (hit) {
+          L = __ffs(hit) - 1;
+        } else {
+          const unsigned nz = __ballot_sync(0xFFFFFFFFu, sl > 0.f);
+          L = nz ? 31 - __clz(nz) : 0;
+          last = true;
         }
-      }
-      float inc2 = acc;
+        int sel = -1;
+        float rem2 = 0.f;
+        if (lane == L) {
+          float run = excl;
+          int slast = -1;
+          for (int j = 0; j < kSegPerLane; ++j) {
+            const int s = lane * kSegPerLane + j;
+            if (s >= nseg) break;
+            const float vs = S.seg[s];
+            if (vs > 0.f) slast = s;
+            if (!last && sel < 0 && vs > 0.f && run + vs > rem) { sel = s; rem2 = __fsub_rn(rem, run); }
+            run += vs;
+          }
+          if (sel < 0) { sel = slast; last = true; }
+          if (sel < 0) sel = 0;
+        }
+        sel = __shfl_sync(0xFFFFFFFFu, sel, L);
+        rem2 = __shfl_sync(0xFFFFFFFFu, rem2, L);
+        last = __shfl_sync(0xFFFFFFFFu, last, L);
+        // within the segment: one vector per lane
+        const int v = sel * 32 + lane;
+        float ev[N];
+        float acc = 0.f;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xFFFFFFFFu, inc2, o);
-        if (lane >= o) inc2 += y;
-      }
-      float exc2 = __shfl_up_sync(0xFFFFFFFFu, inc2, 1);
-      if (lane == 0) exc2 = 0.f;
-      const unsigned hit2 = last ? 0u : __ballot_sync(0xFFFFFFFFu, acc > 0.f && inc2 > rem2);
-      int L2;
-      if (hit2) {
-        L2 = __ffs(hit2) - 1;
-      } else {
-        const unsigned nz = __ballot_sync(0xFFFFFFFFu, acc > 0.f);
-        L2 = nz ? 31 - __clz(nz) : 0;
-      }
-      if (lane == L2) {
-        int pick = -1, lastpos = -1;
-        float run = exc2;
+        for (int j = 0; j < N; ++j) ev[j] = 0.f;
+        if (v < nvec) {
+          const uint4 q = kv4[v];
+          uint32_t k[N];
+          KV<KB>::unpack(q, k);
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-          if (ev[j] > 0.f) {
-            lastpos = j;
-            run += ev[j];
-            if (hit2 && pick < 0 && run > rem2) pick = j;
+          for (int j = 0; j < N; ++j) {
+            if (k[j] >= kdraw) ev[j] = mass_of(C::value(k[j]), T, rT, M);
+            acc += ev[j];
           }
         }
-        if (pick < 0) pick = lastpos;
-        if (pick < 0) pick = 0;
-        result = c0 + v * N + pick;
+        float inc2 = acc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xFFFFFFFFu, inc2, o);
+          if (lane >= o) inc2 += y;
+        }
+        float exc2 = __shfl_up_sync(0xFFFFFFFFu, inc2, 1);
+        if (lane == 0) exc2 = 0.f;
+        const unsigned hit2 = last ? 0u : __ballot_sync(0xFFFFFFFFu, acc > 0.f && inc2 > rem2);
+        int L2;
+        if (hit2) {
+          L2 = __ffs(hit2) - 1;
+        } else {
+          const unsigned nz = __ballot_sync(0xFFFFFFFFu, acc > 0.f);
+          L2 = nz ? 31 - __clz(nz) : 0;
+        }
+        if (lane == L2) {
+          int pick = -1, lastpos = -1;
+          float run = exc2;
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            if (ev[j] > 0.f) {
+              lastpos = j;
+              run += ev[j];
+              if (hit2 && pick < 0 && run > rem2) pick = j;
+            }
+          }
+          if (pick < 0) pick = lastpos;
+          if (pick < 0) pick = 0;
+          result = c0 + v * N + pick;
+        }
       }
     }
     if (rsel < 0) {
       // no finite mass anywhere: fall back to the lowest index of the row max
-      // (every CTA reaches here; kmax is in the CTA whose first_idx is least)
       int first = INT_MAX;
       for (int i = tid; i < n; i += kThreads)
         if (static_cast<uint32_t>(keys[i]) == kmax) { first = i; break; }
@@ -1043,7 +1177,8 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   }
 
   if (result >= 0) P.out[row] = min(result, P.V - 1);
-  cluster_wait();  // every peer is done reading this CTA's shared memory
+  __syncthreads();  // converged warps for the aligned cluster barrier
+  cluster_wait();   // every peer is done reading this CTA's shared memory
 
   if (!P.uniforms && rank == 0 && tid == 0) {
     // the last cluster to finish advances the Philox offset; every cluster
