@@ -9,8 +9,8 @@ A step is one sampler launch over the whole batch.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
 
 native: K launches timed with CUDA events on the launching stream, inputs
-rotating through 8 device copies (311 MB > 126 MB L2) so every launch reads
-its logits from HBM.  ``e2e`` repeats the step through the public API with
+rotating through enough device copies to hold 3x the 126 MB L2 (11 at C2,
+408 MiB) so every launch reads its logits from HBM.  ``e2e`` repeats the step through the public API with
 the logits in pinned host memory: H2D copy, launch, D2H of the ids.
 reference: the reference's CPU sampling path (torch port, all host threads).
 Under torchrun each rank samples its own batch (batch-sharded, no collective);

@@ -241,3 +241,10 @@ def _sample_op_cuda(logits, temperature, top_k, top_p, uniforms, philox_state, r
 
 
 _LIB.impl("sample", _sample_op_cuda, "CUDA")
+
+
+@torch.library.register_fake("ecah::sample")
+def _sample_op_fake(logits, temperature, top_k, top_p, uniforms, philox_state, rep_factor, freq_pen, pres_pen,
+                    row_slot, slot_len, hist_tok, hist_cnt, hist_mval, hist_cap, flags, out, workspace):
+    # writes only into `out` (and the Philox offset / workspace); no new tensors
+    return None
