@@ -21,7 +21,8 @@ STATUS = {0: "ok", 1: "null pointer", 2: "dtype", 3: "shape", 4: "workspace", 5:
 
 # exported symbols declared in include/ecah_sampler.h
 EXPORTS = ("ecah_sampler_abi_version", "ecah_status_string", "ecah_sampler_workspace_bytes",
-           "ecah_sampler_launch", "ecah_hist_update", "ecah_philox_uniforms")
+           "ecah_sampler_launch", "ecah_hist_update", "ecah_philox_uniforms",
+           "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes")
 
 
 class SamplerArgs(ctypes.Structure):
@@ -61,6 +62,10 @@ def lib():
         L.ecah_sampler_workspace_bytes.argtypes = [c_int32, c_int32, c_int32]
         L.ecah_sampler_launch.restype = c_int32
         L.ecah_sampler_launch.argtypes = [ctypes.POINTER(SamplerArgs), c_void_p]
+        L.ecah_sampler_launch_noalloc.restype = c_int32
+        L.ecah_sampler_launch_noalloc.argtypes = [ctypes.POINTER(SamplerArgs), c_void_p]
+        L.ecah_sampler_noalloc_scratch_bytes.restype = c_size_t
+        L.ecah_sampler_noalloc_scratch_bytes.argtypes = []
         L.ecah_hist_update.restype = c_int32
         L.ecah_hist_update.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,

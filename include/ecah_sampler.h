@@ -148,6 +148,19 @@ ECAH_API int ecah_hist_update(const int32_t* ids, int32_t batch, const int32_t* 
 ECAH_API int ecah_philox_uniforms(uint64_t* philox_state, int32_t batch, float* out,
                          int32_t advance, void* stream);
 
+/* ecah_sampler_launch without a caller workspace, for callers that cannot
+ * allocate device memory at sampling time (a runtime that owns all device
+ * memory through its own pool, an FFI caller with no CUDA allocator).  No
+ * counterpart in the reference: FlashInfer's sampler allocates its own state.
+ * Scratch is a fixed array of ecah_sampler_noalloc_scratch_bytes() bytes in
+ * the library's device memory, held on every GPU that loads the library until
+ * exit; shapes whose workspace exceeds it get ECAH_ERR_WORKSPACE.  The first
+ * call on a device looks up the array's address (make it outside stream
+ * capture); calls share the array, so calls overlapping on the GPU race.
+ * args->workspace and args->workspace_bytes are ignored. */
+ECAH_API int ecah_sampler_launch_noalloc(const ecah_sampler_args* args, void* stream);
+ECAH_API size_t ecah_sampler_noalloc_scratch_bytes(void);
+
 #ifdef __cplusplus
 }
 #endif
