@@ -8,9 +8,10 @@ A step is one sampler launch over the whole batch.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
 
-native: K launches timed with CUDA events on the launching stream, inputs
-rotating through enough device copies to hold 3x the 126 MB L2 (11 at C2,
-408 MiB) so every launch reads its logits from HBM.  ``e2e`` repeats the step through the public API with
+native: K launches, replayed from CUDA graphs as a graph-captured decode step
+launches them, timed with CUDA events on the replaying stream; inputs rotate
+through enough device copies to hold 3x the 126 MB L2 (11 at C2, 408 MiB) so
+every launch reads its logits from HBM.  ``e2e`` repeats the step through the public API with
 the logits in pinned host memory: H2D copy, launch, D2H of the ids.
 reference: the reference's CPU sampling path (torch port, all host threads).
 Under torchrun each rank samples its own batch (batch-sharded, no collective);
@@ -193,14 +194,35 @@ def run_native(a):
     for i in range(a.warmup):
         step(i)
     torch.cuda.synchronize()
+    # the timed steps run as CUDA-graph replays (how a graph-captured decode
+    # step launches the sampler): `chunk` launches per graph on rotating
+    # inputs, plus one graph for the remainder, exactly a.steps launches
+    chunk = min(a.steps, 2 * nbuf)
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for i in range(n):
+                step(i)
+        return g
+
+    g_full = capture(chunk)
+    rem = a.steps % chunk
+    g_rem = capture(rem) if rem else None
+    g_full.replay()
+    torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         ev0.record(stream)
-        for i in range(a.steps):
-            step(i)
+        for _ in range(a.steps // chunk):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
         ev1.record(stream)
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
@@ -261,13 +283,16 @@ def run_native(a):
             "config": {"workload": "c2_mixed B=128 V=151936 fp16 (configs[1])", "batch_per_gpu": B,
                        "vocab": V, "l2": f"inputs rotate through {nbuf} device copies "
                        f"({nbuf * bytes_in / 2**20:.0f} MiB > 126 MiB L2)",
-                       "parallelism": f"batch-sharded x{ws}" if ws > 1 else "single GPU"},
+                       "parallelism": f"batch-sharded x{ws}" if ws > 1 else "single GPU",
+                       "launch": f"CUDA-graph replays of {chunk} sampler launches"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke},
-            "gpu_launches": a.steps,
+            # one kernel per sampler launch at B >= 96 (one CTA per row), two below
+            # (chunk scan + row finish); no other kernels run in the timed region
+            "gpu_launches": a.steps * (1 if B >= 96 else 2),
             "clocks": clk.summary(),
         }
         if ws == 1 and not a.no_cpu_baseline:
@@ -283,6 +308,7 @@ def run_native(a):
                 "value": rows * n / dt, "unit": "rows/s", "cores": threads, "kind": "port",
                 "sample": f"{rows} group-interleaved rows of the workload, {n} repetitions in {dt:.1f} s "
                           f"(torch CPU port of the reference path, {threads} threads)"}
+    del g_full, g_rem
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

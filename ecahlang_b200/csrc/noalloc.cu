@@ -24,6 +24,9 @@
 
 #include "../../include/ecah_sampler.h"
 
+// sampler.cu: the least workspace ecah_sampler_launch accepts (not exported)
+extern "C" size_t ecah_internal_min_workspace_bytes(void);
+
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 256;
@@ -62,8 +65,8 @@ int ecah_sampler_launch_noalloc(const ecah_sampler_args* a, void* stream) {
   if (a->abi_version != ECAH_SAMPLER_ABI_VERSION) return ECAH_ERR_ABI;
   if (a->dtype < ECAH_DTYPE_F16 || a->dtype > ECAH_DTYPE_F32) return ECAH_ERR_DTYPE;
   if (a->batch < 0 || a->vocab < 1) return ECAH_ERR_SHAPE;
-  if (ecah_sampler_workspace_bytes(a->batch, a->vocab, a->dtype) > kNoAllocScratchBytes)
-    return ECAH_ERR_WORKSPACE;  // this shape needs more scratch than the library holds
+  if (ecah_internal_min_workspace_bytes() > kNoAllocScratchBytes)
+    return ECAH_ERR_WORKSPACE;  // the launch needs more scratch than the library holds
   if (a->batch == 0) return ECAH_OK;
   void* scratch = scratch_for_current_device();
   if (!scratch) return ECAH_ERR_LAUNCH;

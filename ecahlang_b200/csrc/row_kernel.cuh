@@ -1,0 +1,1004 @@
+// Row-per-CTA token sampler for sm_100a: one 1024-thread CTA owns a whole
+// row, streams it from HBM through a four-stage cp.async pipeline (32 KB
+// rounds), keeps every running quantity on chip and finishes the row without
+// talking to any other CTA.
+//
+// During the stream, per row mode (16-bit keys: fp16/bf16 logits):
+//   - every row: per-thread running (max key, lowest index holding it);
+//   - rows with top-k (k <= kMaxN) or top-p: a candidate buffer in shared
+//     memory holding, in vocab order, every entry whose key is >= a running
+//     floor f.  f starts from a 256-bin histogram of the first round and is
+//     raised, when the buffer would overflow, to the N-th largest key of the
+//     buffer and the round's survivors (N = k, or kDenseN for top-p-only
+//     rows); the buffer always holds exactly the
+//     entries seen so far with key >= f, so every entry of the row at or above
+//     the final f is a candidate;
+//   - rows without top-k: softmax mass sum exp(z - q) per thread against a
+//     running per-thread reference q (online softmax), and for rows that draw
+//     from the whole distribution also per (round, warp) segment sums.
+// After the stream the row max M, the thresholds (exact per-key counts of the
+// candidates, as in the cluster kernel's window path) and the draw (inverse
+// CDF over the candidates in vocab order, or over segment sums and then one
+// re-loaded 512-entry segment) need no further HBM traffic.  Rows whose
+// thresholds fall below the candidate floor re-stream the row and run a
+// two-digit (8 | 8 bit) radix select.
+//
+// Op order, masses (mass_of), tie floors and zero-mass cut are those of the
+// cluster kernel (sampler_kernel.cuh).
+#pragma once
+
+#include "stream_kernel.cuh"
+
+namespace ecah {
+namespace rk {
+
+constexpr int kT = 1024;                  // threads per CTA
+constexpr int kNW = kT / 32;              // warps
+constexpr int kEPT = 16;                  // entries per thread per round
+constexpr int kRound = kT * kEPT;         // entries per round (32 KB of fp16)
+constexpr int kRVecs = kRound / 8;        // 16-byte vectors per round
+constexpr int kStages = 4;                // rounds in flight while one is processed: 3
+constexpr int kCB = 8192;                 // candidate buffer entries
+constexpr int kMaxN = kCB / 2;            // largest candidate target
+constexpr int kDenseN = 4096;             // candidate target of top-p-only rows
+constexpr int kHB = 4096;                 // finishing histogram: keys below the row max
+constexpr int kMaxRounds = 32;            // vocab <= 32 * 16384
+constexpr int kSegs = kMaxRounds * kNW;   // (round, warp) segments of 512 entries
+// fallback level-0 fixed point: a mass <= 1 times 2^22 stays below the 2^23
+// to_fixed needs, and a lane's slot sums at most 16 * 32 masses (< 2^32)
+constexpr float kFx = 4194304.0f;
+constexpr float kFxInv = 1.0f / 4194304.0f;
+
+struct RSmem {
+  uint4 stage[kStages][kRVecs];   // pipeline; after the stream: finishing histograms
+  unsigned lp[256 * 32];          // lane-private 256-bin histograms
+  uint16_t ckey[kCB];             // candidates: key
+  uint32_t cidx[kCB];             //             row index
+  float ss[kSegs];                // segment masses relative to a common reference
+  unsigned h256[256];
+  unsigned red[2][kNW];           // reduction scratch, alternating
+  int wcnt[2][kNW];
+  int ib[16];
+  float fb[16];
+};
+
+// ------------------------------------------------------------ reductions
+// Every thread of the CTA calls them in the same order; `ph` alternates the
+// scratch so no trailing barrier is needed.
+__device__ __forceinline__ unsigned rmax_u(unsigned v, RSmem& S, int& ph) {
+  v = __reduce_max_sync(0xFFFFFFFFu, v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) S.red[ph][warp] = v;
+  __syncthreads();
+  unsigned m = __reduce_max_sync(0xFFFFFFFFu, S.red[ph][lane]);
+  ph ^= 1;
+  return m;
+}
+
+__device__ __forceinline__ unsigned rmin_u(unsigned v, RSmem& S, int& ph) {
+  v = __reduce_min_sync(0xFFFFFFFFu, v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) S.red[ph][warp] = v;
+  __syncthreads();
+  unsigned m = __reduce_min_sync(0xFFFFFFFFu, S.red[ph][lane]);
+  ph ^= 1;
+  return m;
+}
+
+// sum in warp order, then lane order (deterministic)
+__device__ __forceinline__ float rsum_f(float v, RSmem& S, int& ph) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) S.red[ph][warp] = __float_as_uint(v);
+  __syncthreads();
+  float t = warp_sum(__uint_as_float(S.red[ph][lane]));
+  ph ^= 1;
+  return t;
+}
+
+// exclusive prefix of v over threads in thread order; *total = sum
+__device__ __forceinline__ int rscan_i(int v, RSmem& S, int& ph, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) S.wcnt[ph][warp] = incl;
+  __syncthreads();
+  const int wv = S.wcnt[ph][lane];
+  int winc = wv;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, winc, o);
+    if (lane >= o) winc += y;
+  }
+  const int base = __shfl_sync(0xFFFFFFFFu, winc - wv, warp);
+  *total = __shfl_sync(0xFFFFFFFFu, winc, 31);
+  ph ^= 1;
+  return base + incl - v;
+}
+
+__device__ __forceinline__ float rscan_f(float v, RSmem& S, int& ph, float* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) S.red[ph][warp] = __float_as_uint(incl);
+  __syncthreads();
+  const float wv = __uint_as_float(S.red[ph][lane]);
+  float winc = wv;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xFFFFFFFFu, winc, o);
+    if (lane >= o) winc += y;
+  }
+  const float base = __shfl_sync(0xFFFFFFFFu, winc - wv, warp);
+  *total = __shfl_sync(0xFFFFFFFFu, winc, 31);
+  ph ^= 1;
+  return base + (incl - v);
+}
+
+// key j (0..15) of a thread's 8 packed key words
+#define ECAH_RKEY(w, j) ((((j) & 1) != 0) ? ((w)[(j) >> 1] >> 16) : ((w)[(j) >> 1] & 0xFFFFu))
+
+// ------------------------------------------------------------ the stream
+// Round r of `row`: entries [r * kRound, ...) of the row, n of them valid.
+__device__ __forceinline__ int round_len(int V, int r) { return min(kRound, V - r * kRound); }
+
+__device__ __forceinline__ void issue_round(const KParams& P, uint4* st, int row, int r) {
+  if (!P.vec_ok) return;
+  const int n = round_len(P.V, r);
+  const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
+                                                   static_cast<long long>(row) * P.row_stride +
+                                                   static_cast<long long>(r) * kRound);
+  const int nfull = n >> 3;
+  for (int v = threadIdx.x; v < nfull; v += kT) cp_async16(st + v, s4 + v);
+}
+
+// Ragged tail / unaligned rows with plain loads, padding (key 0), penalty
+// patch.  Returns with the stage complete for every thread.
+template <int DT>
+__device__ void complete_round(const KParams& P, uint4* st, int row, int r) {
+  using Dt = DType<DT>;
+  const int tid = threadIdx.x;
+  const int n = round_len(P.V, r);
+  const int c0 = r * kRound;
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
+  uint16_t* raw = reinterpret_cast<uint16_t*>(st);
+  const int done = P.vec_ok ? ((n >> 3) << 3) : 0;
+  const bool tail = done < kRound;
+  if (tail) {
+    for (int i = done + tid; i < kRound; i += kT) raw[i] = (i < n) ? src[i] : static_cast<uint16_t>(0xFFFFu);
+    __syncthreads();
+  }
+  if (P.row_slot) {
+    const int slot = P.row_slot[row];
+    if (slot >= 0 && slot < P.num_slots) {
+      const int len = min(P.slot_len[slot], P.hist_cap);
+      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+      const long long base = static_cast<long long>(slot) * P.hist_cap;
+      for (int h = tid; h < len; h += kT) {
+        const int tok = P.hist_tok[base + h];
+        const int cnt = P.hist_cnt[base + h];
+        const int li = tok - c0;
+        if (cnt <= 0 || li < 0 || li >= n) continue;
+        const float x = Dt::to_f32(raw[li]);
+        const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
+        raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Two 16-bit raws -> two order-preserving keys (key16 on each half): prmt
+// replicates each half's sign bit over the half, one lop3 applies it.
+__device__ __forceinline__ uint32_t keys2(uint32_t w) {
+  uint32_t m;
+  asm("prmt.b32 %0, %1, 0, 0xBB99;" : "=r"(m) : "r"(w));
+  return w ^ (m | 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t max16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t min16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// per half of a key word: 1 where key >= f, else 0 (fm2 = (f - 1) in both
+// halves, f >= 1): max(key, f - 1) - (f - 1) is positive exactly there, and
+// no half borrows from the other
+__device__ __forceinline__ uint32_t surv2(uint32_t w, uint32_t fm2) {
+  return min16x2(max16x2(w, fm2) - fm2, 0x00010001u);
+}
+
+// the two logits of a raw word as float32 (exact)
+template <int DT> __device__ __forceinline__ float2 vals2(uint32_t w);
+template <> __device__ __forceinline__ float2 vals2<ECAH_DTYPE_F16>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <> __device__ __forceinline__ float2 vals2<ECAH_DTYPE_BF16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// this thread's 16 raw logits (entries 16*tid .. 16*tid+15 of the round) and keys
+__device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8]) {
+  const uint4 a = st[2 * threadIdx.x], b = st[2 * threadIdx.x + 1];
+  raw[0] = a.x; raw[1] = a.y; raw[2] = a.z; raw[3] = a.w;
+  raw[4] = b.x; raw[5] = b.y; raw[6] = b.z; raw[7] = b.w;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w[j] = keys2(raw[j]);
+}
+
+// entries e0 .. e0+15 of the row read from global memory with the
+// repetition-penalty patch applied (NaN past the row end)
+template <int DT>
+__device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
+  if (P.row_slot) {
+    const int slot = P.row_slot[row];
+    if (slot >= 0 && slot < P.num_slots) {
+      const int len = min(P.slot_len[slot], P.hist_cap);
+      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+      const long long hb = static_cast<long long>(slot) * P.hist_cap;
+      for (int h = 0; h < len; ++h) {
+        const int li = P.hist_tok[hb + h] - e0;
+        const int cn = P.hist_cnt[hb + h];
+        if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
+        const float m = P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf);
+#pragma unroll
+        for (int j = 0; j < kEPT; ++j)
+          if (j == li) yv[j] = DType<DT>::round(__fdiv_rn(yv[j], m));
+      }
+    }
+  }
+}
+
+// Streams the whole row through the pipeline and calls fn(r, raw, w, nv)
+// once per round with the thread's raw words and keys (nv of its 16 entries
+// are in the row; the rest are padding, key 0); fn may use barriers (every
+// thread calls it).  The next rounds are already in flight while fn runs.
+template <int DT, typename Fn>
+__device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
+  const int R = (P.V + kRound - 1) / kRound;
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < R) issue_round(P, S.stage[s], row, s);
+    cp_async_commit();
+  }
+  for (int r = 0; r < R; ++r) {
+    cp_async_wait_group<kStages - 2>();
+    // round r landed for every thread, and every thread is done with round
+    // r - 1, whose stage the next copy reuses
+    __syncthreads();
+    const int nx = r + kStages - 1;
+    if (nx < R) issue_round(P, S.stage[nx % kStages], row, nx);
+    cp_async_commit();
+    uint4* st = S.stage[r % kStages];
+    complete_round<DT>(P, st, row, r);
+    uint32_t raw[8], w[8];
+    round_load(st, raw, w);
+    const int nv = max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
+    fn(r, raw, w, nv);
+  }
+  cp_async_wait_group<0>();
+  __syncthreads();
+}
+
+// -------------------------------------------------------------- selection
+// Lane-private 256-bin counts (S.lp) -> S.h256.  Barriers on both sides.
+__device__ __forceinline__ void lp_zero(RSmem& S) {
+  uint4* p = reinterpret_cast<uint4*>(S.lp);
+  for (int i = threadIdx.x; i < 256 * 32 / 4; i += kT) p[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+}
+__device__ __forceinline__ void lp_reduce(RSmem& S) {
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < 256) {
+    unsigned acc = 0u;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) acc += S.lp[(t << 5) | ((j + t) & 31)];
+    S.h256[t] = acc;
+  }
+  __syncthreads();
+}
+
+// Among bins 255..0 (descending), the first whose running count reaches n;
+// -1 if the total stays below n.  *above = count of the bins above it.
+// Warp 0 computes, everyone gets the result (barrier inside).
+__device__ __forceinline__ int h256_select_desc(RSmem& S, unsigned n, unsigned* above) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    unsigned v[8], s = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { v[j] = S.h256[255 - (lane * 8 + j)]; s += v[j]; }
+    unsigned incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= n);
+    int bin = -1;
+    unsigned ab = 0u;
+    if (hit) {
+      const int L = __ffs(hit) - 1;
+      if (lane == L) {
+        unsigned acc = incl - s;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (bin < 0 && acc + v[j] >= n) { bin = 255 - (lane * 8 + j); ab = acc; }
+          acc += v[j];
+        }
+      }
+      bin = __shfl_sync(0xFFFFFFFFu, bin, L);
+      ab = __shfl_sync(0xFFFFFFFFu, ab, L);
+    }
+    if (lane == 0) { S.ib[14] = bin; S.ib[15] = static_cast<int>(ab); }
+  }
+  __syncthreads();
+  *above = static_cast<unsigned>(S.ib[15]);
+  return S.ib[14];
+}
+
+// Among bins 0..nb-1 (ascending), the first whose running count reaches n;
+// -1 if the total stays below n.  *above = count of the bins before it.
+__device__ __forceinline__ int h256_select_asc(RSmem& S, unsigned n, unsigned* above) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    unsigned v[8], s = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { v[j] = S.h256[lane * 8 + j]; s += v[j]; }
+    unsigned incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= n);
+    int bin = -1;
+    unsigned ab = 0u;
+    if (hit) {
+      const int L = __ffs(hit) - 1;
+      if (lane == L) {
+        unsigned acc = incl - s;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (bin < 0 && acc + v[j] >= n) { bin = lane * 8 + j; ab = acc; }
+          acc += v[j];
+        }
+      }
+      bin = __shfl_sync(0xFFFFFFFFu, bin, L);
+      ab = __shfl_sync(0xFFFFFFFFu, ab, L);
+    }
+    if (lane == 0) { S.ib[14] = bin; S.ib[15] = static_cast<int>(ab); }
+  }
+  __syncthreads();
+  *above = static_cast<unsigned>(S.ib[15]);
+  return S.ib[14];
+}
+
+// N-th largest key among the candidate buffer [0, fill) and this round's
+// entries with key >= f (N <= their number); kref >= every one of those keys.
+// Bins are measured down from kref, so the counted keys spread over many:
+// 256 bins of 2^s keys give the lowest key of the bin where N is reached (a
+// floor keeping at least N); only when that floor would not rise above f are
+// the 2^s keys of the bin counted one by one for the exact N-th largest.
+__device__ unsigned cand_nth(RSmem& S, int fill, const uint32_t (&w)[8], int nv, unsigned f, unsigned kref,
+                             unsigned N) {
+  const uint32_t lane = threadIdx.x & 31;
+  int sh = 0;
+  while (((kref - f) >> sh) >= 256u) ++sh;
+  lp_zero(S);
+  for (int i = threadIdx.x; i < fill; i += kT) atomicAdd(&S.lp[(((kref - S.ckey[i]) >> sh) << 5) | lane], 1u);
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) {
+    const uint32_t key = ECAH_RKEY(w, j);
+    if (j < nv && key >= f) atomicAdd(&S.lp[(((kref - key) >> sh) << 5) | lane], 1u);
+  }
+  lp_reduce(S);
+  unsigned above;
+  const int b1 = h256_select_asc(S, N, &above);
+  if (sh == 0 || b1 < 0) return kref - static_cast<unsigned>(max(b1, 0));
+  // the lowest key of bin b1 keeps at least N (and the whole bin) when it lies above f
+  const unsigned lowest = kref - ((static_cast<unsigned>(b1) << sh) + ((1u << sh) - 1u));
+  if (kref >= ((static_cast<unsigned>(b1) << sh) + ((1u << sh) - 1u)) && lowest > f) return lowest;
+  const unsigned msk = (1u << sh) - 1u;
+  lp_zero(S);
+  for (int i = threadIdx.x; i < fill; i += kT) {
+    const unsigned d = kref - S.ckey[i];
+    if (static_cast<int>(d >> sh) == b1) atomicAdd(&S.lp[((d & msk) << 5) | lane], 1u);
+  }
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) {
+    const uint32_t key = ECAH_RKEY(w, j);
+    const unsigned d = kref - key;
+    if (j < nv && key >= f && static_cast<int>(d >> sh) == b1) atomicAdd(&S.lp[((d & msk) << 5) | lane], 1u);
+  }
+  lp_reduce(S);
+  unsigned ab2;
+  const int b2 = h256_select_asc(S, N - above, &ab2);
+  return kref - ((static_cast<unsigned>(b1) << sh) + static_cast<unsigned>(max(b2, 0)));
+}
+
+// keep the buffer entries with key >= f, in order; returns the new fill
+__device__ int cand_compact(RSmem& S, int fill, unsigned f, int& ph) {
+  // entries 8*tid .. 8*tid+7 (fill <= kCB = 8 * kT)
+  const int b = threadIdx.x * 8;
+  uint16_t k[8];
+  uint32_t ix[8];
+  int cnt = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool in = b + j < fill;
+    k[j] = in ? S.ckey[b + j] : 0;
+    ix[j] = in ? S.cidx[b + j] : 0u;
+    cnt += (in && k[j] >= f) ? 1 : 0;
+  }
+  int total;
+  const int off = rscan_i(cnt, S, ph, &total);
+  __syncthreads();  // everyone has read its entries before they are overwritten
+  int o = off;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (b + j < fill && k[j] >= f) { S.ckey[o] = k[j]; S.cidx[o] = ix[j]; ++o; }
+  }
+  __syncthreads();
+  return total;
+}
+
+// ------------------------------------------------------ per-round helpers
+// mass of an entry relative to reference q (scaled like z): mass_of with
+// the T == 1 shortcut (z = y exactly, as the divide gives)
+__device__ __forceinline__ float emass(float y, float T, float rT, float q, bool t1) {
+  return t1 ? ex2_approx(__fmul_rn(__fsub_rn(y, q), kLog2e)) : mass_of(y, T, rT, q);
+}
+
+// ------------------------------------------------------------ the kernel
+template <int DT>
+__global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
+  using C = Codec<DT, 16>;
+  extern __shared__ __align__(16) unsigned char dsm[];
+  RSmem& S = *reinterpret_cast<RSmem*>(dsm);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = (P.V + kRound - 1) / kRound;
+
+  for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
+    int ph = 0;
+    const float T = P.temperature[row];
+    const int kk = P.top_k[row];
+    const int k_eff = (kk <= 0 || kk >= P.V) ? P.V : kk;
+    const float pp = P.top_p[row];
+    const bool topk = k_eff < P.V;
+    const bool topp = (pp > 0.f && pp < 1.f);
+    const bool sampled = T > 0.f;
+    const bool t1 = (T == 1.0f);
+    const float rT = __frcp_rn(T);
+    const int N = !sampled ? 0 : (topk ? (k_eff <= kMaxN ? k_eff : 0) : (topp ? kDenseN : 0));
+    const bool mass_all = sampled && !topk;        // S over the whole row
+    const bool segs = mass_all && !topp;           // draw from segment sums
+
+    // running state
+    unsigned best = 0u;       // thread max key
+    int bround = 0;           // first round where this thread met it
+    float q0 = 0.f;           // row mass reference: z of the first round's max
+    float sacc = 0.f;         // thread mass relative to q0
+    unsigned f = 0u;          // candidate floor
+    int fill = 0;
+    bool overflow = (N == 0);
+
+    stream_row<DT>(P, S, row, [&](int r, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+      uint32_t m2 = w[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) m2 = max16x2(m2, w[j]);
+      const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);  // padding keys are 0
+      if (tm > best) { best = tm; bround = r; }
+      uint32_t k0 = 0u;  // round-0 max (round 0 only)
+      if (r == 0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
+
+      if (mass_all) {
+        if (r == 0) q0 = __fdiv_rn(C::value(k0), T);
+        // NaN masses (padding, NaN logits) drop out through fmaxf
+        float rs = 0.f;
+        if (t1) {
+          const float nq = -q0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 y = vals2<DT>(raw[j]);
+            rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.x, nq), kLog2e)), 0.f);
+            rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.y, nq), kLog2e)), 0.f);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 y = vals2<DT>(raw[j]);
+            rs += fmaxf(mass_of(y.x, T, rT, q0), 0.f);
+            rs += fmaxf(mass_of(y.y, T, rT, q0), 0.f);
+          }
+        }
+        sacc += rs;
+        if (segs) {
+          const float ws = warp_sum(rs);
+          if (lane == 0) S.ss[r * kNW + warp] = ws;
+        }
+      }
+
+      if (!overflow) {
+        if (r == 0) {
+          // first floor: counts of the 4096 keys below the round's max k0 in
+          // 256 bins of 16; the lowest key of the bin where N is reached
+          lp_zero(S);
+#pragma unroll
+          for (int j = 0; j < kEPT; ++j) {
+            const uint32_t key = ECAH_RKEY(w, j);
+            const uint32_t d = k0 - key;
+            if (j < nv && d < 4096u) atomicAdd(&S.lp[((d >> 4) << 5) | static_cast<uint32_t>(lane)], 1u);
+          }
+          lp_reduce(S);
+          unsigned above;
+          const int b = h256_select_asc(S, static_cast<unsigned>(N), &above);
+          const uint32_t d = (b >= 0) ? static_cast<uint32_t>(b) * 16u + 15u : 4095u;
+          f = (k0 > d) ? max(k0 - d, 1u) : 1u;  // key 0 is padding
+        }
+        // survivors (key >= f >= 1; padding keys are 0 and never survive)
+        auto count = [&](unsigned fl) -> int {
+          if (!__any_sync(0xFFFFFFFFu, tm >= fl)) return 0;
+          const uint32_t fm2 = (fl - 1u) * 0x00010001u;
+          uint32_t acc = 0u;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc += surv2(w[q], fm2);
+          return static_cast<int>((acc & 0xFFFFu) + (acc >> 16));
+        };
+        int cnt = count(f);
+        int total;
+        int off = rscan_i(cnt, S, ph, &total);
+        if (fill + total > kCB) {
+          // raise the floor toward the N-th largest key of the buffer and this
+          // round's survivors, drop what falls below
+          const unsigned nf = cand_nth(S, fill, w, nv, f, rmax_u(best, S, ph), static_cast<unsigned>(N));
+          if (nf > f) {
+            f = nf;
+            fill = cand_compact(S, fill, f, ph);
+          }
+          cnt = count(f);
+          off = rscan_i(cnt, S, ph, &total);
+          if (fill + total > kCB) overflow = true;
+        }
+        if (!overflow) {
+          if (__any_sync(0xFFFFFFFFu, cnt > 0)) {
+            const uint32_t fm2 = (f - 1u) * 0x00010001u;
+            const uint32_t base = static_cast<uint32_t>(r * kRound + kEPT * tid);
+            int o = fill + off;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t fl = surv2(w[q], fm2);
+              if (fl & 1u) {
+                S.ckey[o] = static_cast<uint16_t>(w[q] & 0xFFFFu);
+                S.cidx[o] = base + 2u * q;
+                ++o;
+              }
+              if (fl >> 16) {
+                S.ckey[o] = static_cast<uint16_t>(w[q] >> 16);
+                S.cidx[o] = base + 2u * q + 1u;
+                ++o;
+              }
+            }
+          }
+          fill += total;
+        }
+      }
+    });
+
+    // ------------------------------------------------ row max and greedy
+    const unsigned kmax = rmax_u(best, S, ph);
+    unsigned firstc = 0xFFFFFFFFu;
+    if (best == kmax) {
+      // the lowest index of kmax among this thread's entries of round bround
+      const int e0 = bround * kRound + kEPT * tid;
+      float yv[kEPT];
+      load16<DT>(P, row, e0, yv);
+#pragma unroll
+      for (int j = 0; j < kEPT; ++j)
+        if (firstc == 0xFFFFFFFFu && e0 + j < P.V && C::from_val(yv[j]) == kmax) firstc = static_cast<unsigned>(e0 + j);
+    }
+    const unsigned first = rmin_u(firstc, S, ph);
+    const float ymax = C::value(kmax);
+    const float M = __fdiv_rn(ymax, T);
+    const bool greedy = !(T > 0.f) || !isfinite(M);
+    int result = static_cast<int>(first == 0xFFFFFFFFu ? 0u : first);
+    RowFin* fin = static_cast<RowFin*>(P.ws_fin) + row;
+    float u = 0.f;
+    if (!greedy) {
+      if (P.uniforms) u = P.uniforms[row];
+      else u = row_uniform(__ldcg(&P.philox_state[0]), __ldcg(&P.philox_state[1]), static_cast<uint64_t>(row));
+    }
+
+    if (greedy) {
+      if (tid == 0) {
+        if (P.row_stats) {
+          float* st = P.row_stats + 4ll * row;
+          st[0] = ymax; st[1] = ymax; st[2] = ymax; st[3] = 1.0f;
+        }
+        fin->M = ymax; fin->Z = 1.0f; fin->kdraw = 0u; fin->mode = 1; fin->idx = result;
+      }
+    } else {
+      const uint32_t key_cut = zero_mass_cut<DT, 16>(M, T);
+      // whole-row mass rescaled to M
+      float S_all = 0.f;
+      bool mass_ok = true;
+      if (mass_all) {
+        // masses were taken relative to q0 <= M: fine unless M - q0 overflows them
+        mass_ok = isfinite(q0) && __fsub_rn(M, q0) < 80.0f;
+        const float s0 = rsum_f(sacc, S, ph);
+        S_all = mass_ok ? __fmul_rn(s0, ex2_approx(__fmul_rn(__fsub_rn(q0, M), kLog2e))) : 0.f;
+        mass_ok = mass_ok && isfinite(S_all);
+      }
+      bool fast = (!overflow || segs) && mass_ok;
+      uint32_t key_lo_k = 0u, key_lo = 0u;
+      unsigned* cnth = reinterpret_cast<unsigned*>(S.stage);   // [kHB] counts, bin b = key kmax - b
+      uint32_t F = f;
+      if (!overflow && (topk || topp)) {
+        if (kmax >= static_cast<uint32_t>(kHB) && F < kmax - static_cast<uint32_t>(kHB - 1))
+          F = kmax - static_cast<uint32_t>(kHB - 1);   // entries below stay out of the histogram
+        for (int i = tid; i < kHB; i += kT) cnth[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < fill; i += kT) {
+          const unsigned key = S.ckey[i];
+          if (key >= F) atomicAdd(&cnth[kmax - key], 1u);
+        }
+        __syncthreads();
+        const int Bmax = static_cast<int>(kmax - F);
+        // top-k: the k-th largest key among the candidates
+        if (topk) {
+          // threads own 4 consecutive bins; running counts in bin order
+          unsigned c4 = 0u;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) c4 += cnth[tid * 4 + j];
+          int tot;
+          const int ex = rscan_i(static_cast<int>(c4), S, ph, &tot);
+          int mine = INT_MAX;
+          if (static_cast<unsigned>(ex) < static_cast<unsigned>(k_eff) &&
+              static_cast<unsigned>(ex) + c4 >= static_cast<unsigned>(k_eff)) {
+            unsigned acc = static_cast<unsigned>(ex);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const unsigned v = cnth[tid * 4 + j];
+              if (mine == INT_MAX && acc + v >= static_cast<unsigned>(k_eff)) mine = tid * 4 + j;
+              acc += v;
+            }
+          }
+          const unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+          if (tot < k_eff || bsel == static_cast<unsigned>(INT_MAX)) {
+            fast = false;
+          } else {
+            if (tid == 0) S.ib[0] = static_cast<int>(tie_floor<DT, 16>(kmax - bsel, T));
+            __syncthreads();
+            key_lo_k = static_cast<uint32_t>(S.ib[0]);
+            if (key_lo_k < F) fast = false;
+          }
+        }
+        key_lo = key_lo_k;
+        if (fast && topp) {
+          const int bk = topk ? static_cast<int>(kmax - key_lo_k) : Bmax;
+          float m4[4];
+          float s4 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int b = tid * 4 + j;
+            const unsigned cn = cnth[b];
+            m4[j] = (b <= bk && cn) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
+            s4 += m4[j];
+          }
+          float tot;
+          const float ex = rscan_f(s4, S, ph, &tot);
+          const float S_K = topk ? tot : S_all;
+          const float target = __fmul_rn(pp, S_K);
+          int mine = INT_MAX;
+          if (s4 > 0.f && ex + s4 >= target) {
+            float acc = ex;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (mine == INT_MAX && m4[j] > 0.f && acc + m4[j] >= target) mine = tid * 4 + j;
+              acc += m4[j];
+            }
+            if (mine == INT_MAX) {
+              // rounding left the target unreached inside this thread: its last non-zero bin
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if (m4[j] > 0.f) mine = tid * 4 + j;
+            }
+          }
+          unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+          const bool reached = tot >= target;
+          if (bsel == static_cast<unsigned>(INT_MAX) && reached) {
+            // the running total reaches the target only after rounding: last non-zero bin
+            int last = -1;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (m4[j] > 0.f) last = tid * 4 + j;
+            bsel = static_cast<unsigned>(static_cast<int>(rmax_u(static_cast<unsigned>(last + 1), S, ph)) - 1);
+          }
+          if (!reached || bsel == static_cast<unsigned>(INT_MAX) || bsel == 0xFFFFFFFFu) {
+            fast = false;
+          } else {
+            if (tid == 0) S.ib[1] = static_cast<int>(max(tie_floor<DT, 16>(kmax - bsel, T), key_lo_k));
+            __syncthreads();
+            key_lo = static_cast<uint32_t>(S.ib[1]);
+            if (key_lo < F) fast = false;
+          }
+        }
+      }
+
+      if (!fast) {
+        // ---------------------------------- fallback: radix select by re-streaming
+        key_lo_k = 0u;
+        if (topk) {
+          lp_zero(S);
+          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j)
+              if (j < nv) atomicAdd(&S.lp[((ECAH_RKEY(w, j) >> 8) << 5) | static_cast<uint32_t>(lane)], 1u);
+          });
+          lp_reduce(S);
+          unsigned above;
+          const int hb = h256_select_desc(S, static_cast<unsigned>(k_eff), &above);
+          lp_zero(S);
+          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j) {
+              const uint32_t key = ECAH_RKEY(w, j);
+              if (j < nv && static_cast<int>(key >> 8) == hb) atomicAdd(&S.lp[((key & 255u) << 5) | static_cast<uint32_t>(lane)], 1u);
+            }
+          });
+          lp_reduce(S);
+          unsigned ab2;
+          const int lb = h256_select_desc(S, static_cast<unsigned>(k_eff) - above, &ab2);
+          if (tid == 0) S.ib[0] = static_cast<int>(tie_floor<DT, 16>((static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(lb), T));
+          __syncthreads();
+          key_lo_k = static_cast<uint32_t>(S.ib[0]);
+        }
+        key_lo = key_lo_k;
+        if (topp) {
+          const uint32_t klo = max(key_lo_k, key_cut);
+          lp_zero(S);
+          float sk = 0.f;
+          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j) {
+              const uint32_t key = ECAH_RKEY(w, j);
+              if (j < nv && key >= klo) {
+                const float e = mass_of(C::value(key), T, rT, M);
+                sk += e;
+                atomicAdd(&S.lp[((key >> 8) << 5) | static_cast<uint32_t>(lane)], to_fixed(e, kFx));
+              }
+            }
+          });
+          const float S_K = rsum_f(sk, S, ph);
+          __syncthreads();
+          float* l0 = reinterpret_cast<float*>(S.stage);
+          if (tid < 256) {
+            unsigned long long acc = 0ull;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
+            l0[tid] = static_cast<float>(acc) * kFxInv;
+          }
+          __syncthreads();
+          const float target = __fmul_rn(pp, S_K);
+          if (tid < 32) {
+            int b; float ab;
+            warp_select_seq<float, 256, true>(l0, target, &b, &ab);
+            if (lane == 0) S.ib[2] = b;
+          }
+          __syncthreads();
+          const int hb = S.ib[2];
+          lp_zero(S);
+          float above = 0.f;
+          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j) {
+              const uint32_t key = ECAH_RKEY(w, j);
+              if (j < nv && key >= klo) {
+                const int kb = static_cast<int>(key >> 8);
+                if (kb == hb) atomicAdd(&S.lp[((key & 255u) << 5) | static_cast<uint32_t>(lane)], 1u);
+                else if (kb > hb) above += mass_of(C::value(key), T, rT, M);
+              }
+            }
+          });
+          const float above_b = rsum_f(above, S, ph);
+          lp_reduce(S);
+          float* m1 = reinterpret_cast<float*>(S.stage);
+          if (tid < 256) {
+            const uint32_t key = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(tid);
+            const unsigned cn = S.h256[tid];
+            m1[tid] = cn ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(key), T, rT, M)) : 0.f;
+          }
+          __syncthreads();
+          if (tid < 32) {
+            int d; float ab;
+            warp_select_seq<float, 256, true>(m1, __fsub_rn(target, above_b), &d, &ab);
+            if (lane == 0) S.ib[3] = static_cast<int>(max(tie_floor<DT, 16>((static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(d), T), key_lo_k));
+          }
+          __syncthreads();
+          key_lo = static_cast<uint32_t>(S.ib[3]);
+        }
+      }
+
+      const uint32_t kdraw = max(key_lo, key_cut);
+      float Z = 0.f;
+      bool none = false;
+      if (fast && (topk || topp)) {
+        // inverse CDF over the candidates, in vocab order (entries 8*tid .. 8*tid+7)
+        float e[8];
+        float s8 = 0.f;
+        const int b0 = tid * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = b0 + j;
+          e[j] = 0.f;
+          if (i < fill) {
+            const uint32_t key = S.ckey[i];
+            if (key >= kdraw) e[j] = mass_of(C::value(key), T, rT, M);
+          }
+          s8 += e[j];
+        }
+        const float ex = rscan_f(s8, S, ph, &Z);
+        const float target = __fmul_rn(u, Z);
+        int mine = INT_MAX, last = -1;
+        float acc = ex;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (e[j] > 0.f) {
+            last = b0 + j;
+            if (mine == INT_MAX && acc + e[j] > target) mine = b0 + j;
+            acc += e[j];
+          }
+        }
+        const unsigned pick = rmin_u(static_cast<unsigned>(mine), S, ph);
+        const unsigned lastp = rmax_u(static_cast<unsigned>(last + 1), S, ph);
+        if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(S.cidx[pick]);
+        else if (lastp > 0u) result = static_cast<int>(S.cidx[lastp - 1u]);
+        else none = true;
+      } else {
+        // segment sums: from the stream (whole distribution) or a re-stream
+        const int nseg = R * kNW;
+        float sref = q0;  // reference of the segment sums
+        if (!(fast && segs)) {
+          stream_row<DT>(P, S, row, [&](int r, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+            float a = 0.f;
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j) {
+              const uint32_t key = ECAH_RKEY(w, j);
+              if (j < nv && key >= kdraw) a += mass_of(C::value(key), T, rT, M);
+            }
+            a = warp_sum(a);
+            if (lane == 0) S.ss[r * kNW + warp] = a;
+          });
+          sref = M;
+        }
+        // per-segment mass relative to M, then the segment holding u * Z
+        const float sc = ex2_approx(__fmul_rn(__fsub_rn(sref, M), kLog2e));
+        float v = 0.f;
+        if (tid < nseg) {
+          const float ss = S.ss[tid];
+          v = (ss > 0.f) ? __fmul_rn(ss, sc) : 0.f;
+        }
+        const float ex = rscan_f(v, S, ph, &Z);
+        const float target = __fmul_rn(u, Z);
+        const int mine = (tid < nseg && v > 0.f && ex + v > target) ? tid : INT_MAX;
+        const unsigned pick = rmin_u(static_cast<unsigned>(mine), S, ph);
+        const unsigned lastp = rmax_u(static_cast<unsigned>(v > 0.f ? tid + 1 : 0), S, ph);
+        int seg;
+        bool take_last = false;
+        if (pick != static_cast<unsigned>(INT_MAX)) seg = static_cast<int>(pick);
+        else if (lastp > 0u) { seg = static_cast<int>(lastp) - 1; take_last = true; }
+        else { seg = -1; none = true; }
+        if (seg >= 0) {
+          // remaining target inside the segment (threads see the same prefix value)
+          if (tid == seg) S.fb[0] = __fsub_rn(target, ex);
+          __syncthreads();
+          const float rem = S.fb[0];
+          // re-load the segment's 512 entries: warp 0, 16 per lane
+          if (warp == 0) {
+            const int r = seg / kNW, sw = seg % kNW;
+            const int e0 = r * kRound + sw * 512 + lane * kEPT;
+            float ev[kEPT];
+            float ls = 0.f;
+            int lastj = -1;
+            float yv[kEPT];
+            load16<DT>(P, row, e0, yv);
+#pragma unroll
+            for (int j = 0; j < kEPT; ++j) {
+              const int i = e0 + j;
+              ev[j] = 0.f;
+              if (i < P.V) {
+                const uint32_t key = C::from_val(yv[j]);
+                if (key >= kdraw) ev[j] = mass_of(yv[j], T, rT, M);
+              }
+              if (ev[j] > 0.f) lastj = j;
+              ls += ev[j];
+            }
+            float incl = ls;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            const float excl = incl - ls;
+            const unsigned hit = take_last ? 0u : __ballot_sync(0xFFFFFFFFu, ls > 0.f && incl > rem);
+            int L;
+            bool last = take_last;
+            if (hit) L = __ffs(hit) - 1;
+            else {
+              const unsigned nz = __ballot_sync(0xFFFFFFFFu, ls > 0.f);
+              L = nz ? 31 - __clz(nz) : 0;
+              last = true;
+            }
+            if (lane == L) {
+              int pk = -1;
+              float run = excl;
+#pragma unroll
+              for (int j = 0; j < kEPT; ++j) {
+                if (pk < 0 && !last && ev[j] > 0.f) {
+                  run += ev[j];
+                  if (run > rem) pk = j;
+                }
+              }
+              if (pk < 0) pk = max(lastj, 0);
+              S.ib[4] = e0 + pk;
+            }
+          }
+          __syncthreads();
+          result = S.ib[4];
+        }
+      }
+      if (none) {
+        // no finite mass anywhere: the lowest index of the row max
+        result = static_cast<int>(first == 0xFFFFFFFFu ? 0u : first);
+      }
+      if (tid == 0) {
+        if (P.row_stats) {
+          float* st = P.row_stats + 4ll * row;
+          st[0] = topk ? C::value(key_lo_k) : -INFINITY;
+          st[1] = (topk || topp) ? C::value(key_lo) : -INFINITY;
+          st[2] = M;
+          st[3] = Z;
+        }
+        fin->M = M; fin->Z = Z; fin->kdraw = kdraw; fin->mode = none ? 2 : 0; fin->idx = result;
+      }
+    }
+
+    if (tid == 0) {
+      P.out[row] = min(result, P.V - 1);
+      if (!P.uniforms) {
+        // the last row to finish advances the Philox offset; every row read
+        // the offset before it arrives here
+        __threadfence();
+        const unsigned prev = atomicAdd(P.done_counter, 1u);
+        if (prev == static_cast<unsigned>(P.B) - 1u) {
+          P.philox_state[1] += 1ull;
+          *P.done_counter = 0u;
+          __threadfence();
+        }
+      }
+    }
+    __syncthreads();  // shared state is reused by the next row
+  }
+}
+
+#undef ECAH_RKEY
+
+}  // namespace rk
+}  // namespace ecah

@@ -1,9 +1,11 @@
 // Host launcher and small kernels of libecah_sampler.so (C ABI in
-// include/ecah_sampler.h).  The sampler kernel itself is in sampler_kernel.cuh.
+// include/ecah_sampler.h).  The sampler kernels are in stream_kernel.cuh (16-bit
+// keys: fp16/bf16 logits without additive penalties, given the full workspace)
+// and sampler_kernel.cuh (everything else).
 
 #include <cstdio>
 
-#include "sampler_kernel.cuh"
+#include "row_kernel.cuh"
 
 namespace ecah {
 
@@ -73,6 +75,68 @@ struct Plan {
 };
 
 static constexpr size_t kMaxDynSmem = 128 * 1024;
+// the cluster kernel's workspace: the Philox completion counter
+static constexpr size_t kMinWorkspace = 256;
+
+// Workspace of the streaming kernels: [0, 256) the Philox completion counter,
+// then chunk summaries, finished-row data and the candidate lists, each
+// region 256-byte aligned.
+struct StreamLayout {
+  int NC;
+  size_t sums, fin, cand, total;
+};
+
+static bool stream_layout(long long B, int V, StreamLayout* L) {
+  if (B < 0 || V < 1) return false;
+  const int NC = (V + kSCH - 1) / kSCH;
+  if (NC > kSMaxChunks) return false;
+  auto a256 = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t b = static_cast<size_t>(B);
+  size_t off = kMinWorkspace;
+  L->sums = off; off += a256(b * NC * sizeof(ChunkSum));
+  L->fin = off; off += a256(b * sizeof(RowFin));
+  L->cand = off; off += a256(b * NC * kSCap * sizeof(unsigned));
+  L->NC = NC;
+  L->total = off;
+  return true;
+}
+
+static bool stream_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
+
+// One CTA per row leaves SMs idle for small batches; below this the rows are
+// split into chunks across all SMs instead (stream_kernel.cuh).
+static constexpr int kRowKernelMinBatch = 96;
+
+// SM count of the current device, looked up once per device.
+static int device_sms() {
+  constexpr int kMaxDev = 64;
+  static int cache[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  if (cache[dev] > 0) return cache[dev];
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  cache[dev] = sms;
+  return sms;
+}
+
+// CTAs of the persistent streaming kernel that fit on the current device at
+// once (occupancy x SM count), looked up once per device and kernel.
+static int stream_resident_ctas(KernelFn fn) {
+  constexpr int kMaxDev = 64;
+  static int cache[2][kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
+  const int which = (fn == stream_scan_kernel<ECAH_DTYPE_F16>) ? 0 : 1;
+  int v = cache[which][dev];
+  if (v > 0) return v;
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, 0) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  v = per_sm * sms;
+  cache[which][dev] = v;
+  return v;
+}
 
 static bool make_plan(int dtype, int V, unsigned flags, Plan* p) {
   const int kb = (dtype == ECAH_DTYPE_F32 || (flags & ECAH_FLAG_FREQ_PRES)) ? 32 : 16;
@@ -118,9 +182,13 @@ const char* ecah_status_string(int s) {
 }
 
 size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype) {
-  (void)batch; (void)vocab; (void)dtype;
-  return 256;
+  StreamLayout L;
+  if (stream_dtype(dtype) && stream_layout(batch, vocab, &L)) return L.total;
+  return kMinWorkspace;
 }
+
+// Not exported: the least workspace any launch accepts (the cluster kernel's).
+size_t ecah_internal_min_workspace_bytes(void) { return kMinWorkspace; }
 
 int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   if (!a) return ECAH_ERR_NULL;
@@ -131,13 +199,9 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   if (!a->logits || !a->temperature || !a->top_k || !a->top_p || !a->out) return ECAH_ERR_NULL;
   if (!a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
   if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
-  if (!a->workspace || a->workspace_bytes < ecah_sampler_workspace_bytes(a->batch, a->vocab, a->dtype))
-    return ECAH_ERR_WORKSPACE;
-  Plan plan;
-  if (!make_plan(a->dtype, a->vocab, a->flags, &plan)) return ECAH_ERR_SHAPE;
-  if (static_cast<long long>(a->batch) * plan.CL > 0x7FFFFFFFLL) return ECAH_ERR_SHAPE;
+  if (!a->workspace || a->workspace_bytes < kMinWorkspace) return ECAH_ERR_WORKSPACE;
 
-  KParams P;
+  KParams P = {};
   P.logits = a->logits;
   P.row_stride = a->row_stride;
   P.B = a->batch;
@@ -162,10 +226,76 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   P.row_stats = a->row_stats;
   P.probs_out = a->probs_out;
   P.done_counter = reinterpret_cast<unsigned*>(a->workspace);
-  P.CL = plan.CL;
-  P.CH = plan.CH;
   const int es = elem_size(a->dtype);
   P.vec_ok = (reinterpret_cast<uintptr_t>(a->logits) % 16 == 0) && ((a->row_stride * es) % 16 == 0);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  // row kernel: 16-bit keys, one CTA per row, for batches that occupy most SMs
+  StreamLayout L;
+  const bool k16 = stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES);
+  if (k16 && a->batch >= kRowKernelMinBatch && a->vocab <= rk::kMaxRounds * rk::kRound &&
+      stream_layout(a->batch, a->vocab, &L) && a->workspace_bytes >= L.total) {
+    unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+    P.NC = L.NC;
+    P.ws_sums = ws + L.sums;
+    P.ws_fin = ws + L.fin;
+    P.ws_cand = reinterpret_cast<unsigned*>(ws + L.cand);
+    const int smem = static_cast<int>(sizeof(rk::RSmem));
+    const int sms = device_sms();
+    if (sms <= 0) return ECAH_ERR_LAUNCH;
+    const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
+    const dim3 all(static_cast<unsigned>(static_cast<long long>(a->batch) * L.NC));
+    if (a->dtype == ECAH_DTYPE_F16) {
+      if (cudaFuncSetAttribute(rk::row_sample_kernel<ECAH_DTYPE_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return ECAH_ERR_LAUNCH;
+      rk::row_sample_kernel<ECAH_DTYPE_F16><<<grid, rk::kT, smem, s>>>(P);
+      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
+    } else {
+      if (cudaFuncSetAttribute(rk::row_sample_kernel<ECAH_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return ECAH_ERR_LAUNCH;
+      rk::row_sample_kernel<ECAH_DTYPE_BF16><<<grid, rk::kT, smem, s>>>(P);
+      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
+    }
+    return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+  }
+
+  // streaming kernel: 16-bit keys and the full workspace
+  if (stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES) && stream_layout(a->batch, a->vocab, &L) &&
+      a->workspace_bytes >= L.total && static_cast<long long>(a->batch) * L.NC <= 0x7FFFFFFFLL) {
+    unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+    P.NC = L.NC;
+    P.ws_sums = ws + L.sums;
+    P.ws_fin = ws + L.fin;
+    P.ws_cand = reinterpret_cast<unsigned*>(ws + L.cand);
+    const long long units = static_cast<long long>(a->batch) * L.NC;
+    const dim3 all(static_cast<unsigned>(units));
+    const dim3 rows(static_cast<unsigned>(a->batch));
+    if (a->dtype == ECAH_DTYPE_F16) {
+      const int resident = stream_resident_ctas(stream_scan_kernel<ECAH_DTYPE_F16>);
+      if (resident <= 0) return ECAH_ERR_LAUNCH;
+      const dim3 grid(static_cast<unsigned>(units < resident ? units : resident));
+      stream_scan_kernel<ECAH_DTYPE_F16><<<grid, kThreads, 0, s>>>(P);
+      stream_finish_kernel<ECAH_DTYPE_F16><<<rows, kThreads, 0, s>>>(P);
+      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
+    } else {
+      const int resident = stream_resident_ctas(stream_scan_kernel<ECAH_DTYPE_BF16>);
+      if (resident <= 0) return ECAH_ERR_LAUNCH;
+      const dim3 grid(static_cast<unsigned>(units < resident ? units : resident));
+      stream_scan_kernel<ECAH_DTYPE_BF16><<<grid, kThreads, 0, s>>>(P);
+      stream_finish_kernel<ECAH_DTYPE_BF16><<<rows, kThreads, 0, s>>>(P);
+      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
+    }
+    return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+  }
+
+  // cluster kernel
+  Plan plan;
+  if (!make_plan(a->dtype, a->vocab, a->flags, &plan)) return ECAH_ERR_SHAPE;
+  if (static_cast<long long>(a->batch) * plan.CL > 0x7FFFFFFFLL) return ECAH_ERR_SHAPE;
+  P.CL = plan.CL;
+  P.CH = plan.CH;
   P.fx_scale = ldexpf(1.0f, plan.fx_log2);
   P.fx_inv = ldexpf(1.0f, -plan.fx_log2);
 
@@ -180,7 +310,7 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   cfg.gridDim = dim3(static_cast<unsigned>(a->batch * plan.CL), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;
-  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = plan.CL;

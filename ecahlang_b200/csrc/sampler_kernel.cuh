@@ -69,6 +69,11 @@ struct KParams {
   float* row_stats;
   float* probs_out;
   unsigned* done_counter;  // workspace word for the Philox offset bump
+  // streaming kernel (stream_kernel.cuh): chunks per row and workspace regions
+  int NC;
+  void* ws_sums;           // [B, NC] chunk summaries
+  unsigned* ws_cand;       // [B, NC, kSCap] candidate lists
+  void* ws_fin;            // [B] finished-row data for the probability kernel
   int CL;                  // CTAs per row (cluster size)
   int CH;                  // vocab entries per CTA (multiple of 8)
   int vec_ok;              // 16-byte aligned rows
@@ -335,6 +340,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }

@@ -12,9 +12,35 @@ DT = {torch.float16: "f16", torch.bfloat16: "bf16", torch.float32: "f32"}
 BOUNDARY = 1e-6     # u / top-p margins below this are reported, not asserted
 
 
+ROW_KERNEL_BATCH = 96   # batches from this size on run one CTA per row
+
+
+def tiled(B):
+    """Copies of a B-row batch that reach the row-per-CTA kernel's batch size."""
+    return -(-ROW_KERNEL_BATCH // B)
+
+
 def run_gpu(x, T, K, P, U, *, history=None, rp=None, f=None, pi=None, freq_pres=False,
-            use_mval=True, probs=False, row_stride=None):
-    """x: CPU [B,V] model dtype.  history: per row (toks, cnts[, mvals]) or None."""
+            use_mval=True, probs=False, row_stride=None, tile=1):
+    """x: CPU [B,V] model dtype.  history: per row (toks, cnts[, mvals]) or None.
+    tile > 1 samples `tile` stacked copies of the batch in one launch (so a
+    small case also runs through the kernel for large batches); every copy
+    must give the same results, and the first copy's are returned."""
+    if tile > 1:
+        B0 = x.shape[0]
+        rep = lambda a: None if a is None else np.tile(np.asarray(a), tile)
+        out = run_gpu(x.repeat(tile, 1), rep(T), rep(K), rep(P), rep(U),
+                      history=None if history is None else list(history) * tile,
+                      rp=rep(rp), f=rep(f), pi=rep(pi), freq_pres=freq_pres, use_mval=use_mval,
+                      probs=probs, row_stride=row_stride)
+        ids, stats, po = out
+        for t in range(1, tile):
+            sl = slice(t * B0, (t + 1) * B0)
+            assert np.array_equal(ids[sl], ids[:B0]), f"copy {t}: ids differ"
+            assert np.array_equal(stats[sl], stats[:B0], equal_nan=True), f"copy {t}: row stats differ"
+            if po is not None:
+                assert np.array_equal(po[sl], po[:B0]), f"copy {t}: probabilities differ"
+        return ids[:B0], stats[:B0], (po[:B0] if po is not None else None)
     dev = torch.device("cuda")
     B, V = x.shape
     if row_stride is not None and row_stride != V:

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from conftest import GOLDEN_CASES, golden_history, load_golden
-from gpu_util import BOUNDARY, compare, run_gpu, run_oracle
+from gpu_util import BOUNDARY, compare, run_gpu, run_oracle, tiled
 from ecahlang_b200 import sampler as S
 from ecahlang_b200 import workloads as W
 from oracle import sampler_oracle as so
@@ -26,9 +26,11 @@ def _golden_tensor(d):
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
 @pytest.mark.parametrize("top_p", [1.0, 0.9, 0.5])
-def test_golden_fixtures(name, top_p):
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_golden_fixtures(name, top_p, big_batch):
     """The reference-pinned fixtures (penalty table, temperatures, top-k with
-    ties) through the CUDA path, with and without top-p."""
+    ties) through the CUDA path, with and without top-p; big_batch stacks
+    copies of the rows so they also run through the large-batch kernel."""
     d = load_golden(name)
     x = _golden_tensor(d)
     B, V = x.shape
@@ -36,7 +38,7 @@ def test_golden_fixtures(name, top_p):
     T, K = d["temperature"], d["top_k"]
     P = np.full(B, top_p, np.float32)
     U = row_uniforms(11, 3, B)
-    gpu = run_gpu(x, T, K, P, U, history=hist, probs=V <= 4096)
+    gpu = run_gpu(x, T, K, P, U, history=hist, probs=V <= 4096, tile=tiled(B) if big_batch else 1)
     orc = run_oracle(x, T, K, P, U, history=hist)
     nb = compare(x, T, K, P, U, gpu, orc, history=hist, probs=gpu[2])
     assert nb <= max(1, B // 8)
@@ -77,16 +79,18 @@ def test_config1_fp32():
     compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, probs=gpu[2])
 
 
-def test_config4_bf16_subset():
-    w = W.config4(seed=0, B=48)
+@pytest.mark.parametrize("B", [48, 128])
+def test_config4_bf16_subset(B):
+    w = W.config4(seed=0, B=B)
     gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, probs=True)
     orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
     compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, probs=gpu[2])
 
 
-@pytest.mark.parametrize("V", [1, 2, 7, 33, 1000, 4097, 20481, 65537])
+@pytest.mark.parametrize("V", [1, 2, 7, 33, 1000, 4097, 16385, 20481, 65537])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
-def test_odd_vocab_sizes(V, dtype):
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_odd_vocab_sizes(V, dtype, big_batch):
     g = torch.Generator().manual_seed(V)
     B = 12
     x = (torch.randn(B, V, generator=g) * 2).to(dtype)
@@ -94,12 +98,13 @@ def test_odd_vocab_sizes(V, dtype):
     K = np.array([0, 1, 3, V, 5, V - 1, 2, V + 5, -1, 10, 1, 0], np.int32)
     P = np.array([1.0, 0.9, 0.5, 0.99, 1.0, 0.3, 1.0, 0.0, 0.7, 1e-6, 0.999999, 0.95], np.float32)
     U = row_uniforms(V, 0, B)
-    gpu = run_gpu(x, T, K, P, U, probs=True)
+    gpu = run_gpu(x, T, K, P, U, probs=True, tile=tiled(B) if big_batch else 1)
     orc = run_oracle(x, T, K, P, U)
     compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
 
 
-def test_unaligned_rows_use_scalar_loads():
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_unaligned_rows_use_scalar_loads(big_batch):
     g = torch.Generator().manual_seed(5)
     B, V = 6, 3001
     x = (torch.randn(B, V, generator=g) * 3).half()
@@ -107,13 +112,14 @@ def test_unaligned_rows_use_scalar_loads():
     K = np.array([0, 10, 100, 0, 1, 50], np.int32)
     P = np.array([0.9, 1.0, 0.8, 1.0, 1.0, 0.5], np.float32)
     U = row_uniforms(1, 1, B)
-    gpu = run_gpu(x, T, K, P, U, row_stride=V + 3)
+    gpu = run_gpu(x, T, K, P, U, row_stride=V + 3, tile=tiled(B) if big_batch else 1)
     orc = run_oracle(x, T, K, P, U)
     compare(x, T, K, P, U, gpu, orc)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
-def test_ties_and_flat_rows(dtype):
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_ties_and_flat_rows(dtype, big_batch):
     g = torch.Generator().manual_seed(9)
     B, V = 16, 30000
     x = torch.round(torch.randn(B, V, generator=g) * 4) / 2   # many exact ties
@@ -125,7 +131,7 @@ def test_ties_and_flat_rows(dtype):
     K = np.array([7, 0, 0, 5, 1, 40, 2, 100, 0, 3, 17, 0, 1000, 2, 9, 0], np.int32)
     P = np.array([1.0, 0.5, 1.0, 0.9, 1.0, 0.6, 0.95, 1.0, 0.5, 1.0, 0.25, 0.75, 0.9, 1.0, 0.3, 0.999], np.float32)
     U = row_uniforms(3, 0, B)
-    gpu = run_gpu(x, T, K, P, U, probs=True)
+    gpu = run_gpu(x, T, K, P, U, probs=True, tile=tiled(B) if big_batch else 1)
     orc = run_oracle(x, T, K, P, U)
     nb = compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
     assert nb <= 2
@@ -159,10 +165,11 @@ def test_philox_device_matches_cpu_twin_and_advances():
     assert st.cpu().tolist() == [0xDEADBEEF12345, 78]
 
 
-def test_sampler_philox_path_and_offset_bump():
+@pytest.mark.parametrize("B", [64, 128])
+def test_sampler_philox_path_and_offset_bump(B):
     dev = torch.device("cuda")
-    w = W.config2(seed=1, B=64, V=5000)
-    smp = S.Sampler(64, 5000, torch.float16, dev, seed=1234)
+    w = W.config2(seed=1, B=B, V=5000)
+    smp = S.Sampler(B, 5000, torch.float16, dev, seed=1234)
     xd = w.logits.to(dev)
     T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
     got = []
@@ -171,16 +178,17 @@ def test_sampler_philox_path_and_offset_bump():
     torch.cuda.synchronize()
     assert smp.philox_state.cpu().tolist() == [1234, 3]
     for off in range(3):
-        U = row_uniforms(1234, off, 64)
-        ids = S.launch(xd, T, K, P, torch.empty(64, dtype=torch.int32, device=dev),
-                       S.new_workspace(64, 5000, torch.float16, dev), uniforms=torch.from_numpy(U).to(dev))
+        U = row_uniforms(1234, off, B)
+        ids = S.launch(xd, T, K, P, torch.empty(B, dtype=torch.int32, device=dev),
+                       S.new_workspace(B, 5000, torch.float16, dev), uniforms=torch.from_numpy(U).to(dev))
         assert torch.equal(ids, got[off])
 
 
-def test_cuda_graph_capture_and_replay():
+@pytest.mark.parametrize("B", [32, 128])
+def test_cuda_graph_capture_and_replay(B):
     dev = torch.device("cuda")
-    w = W.config2(seed=2, B=32, V=151936)
-    smp = S.Sampler(32, w.vocab, torch.float16, dev, seed=99)
+    w = W.config2(seed=2, B=B, V=151936)
+    smp = S.Sampler(B, w.vocab, torch.float16, dev, seed=99)
     xd = w.logits.to(dev)
     T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
     s = torch.cuda.Stream()
@@ -199,9 +207,9 @@ def test_cuda_graph_capture_and_replay():
     torch.cuda.synchronize()
     assert smp.philox_state.cpu().tolist() == [99, 4]
     for i, o in enumerate(outs):
-        U = torch.from_numpy(row_uniforms(99, 1 + i, 32)).to(dev)
-        ref = S.launch(xd, T, K, P, torch.empty(32, dtype=torch.int32, device=dev),
-                       S.new_workspace(32, w.vocab, torch.float16, dev), uniforms=U)
+        U = torch.from_numpy(row_uniforms(99, 1 + i, B)).to(dev)
+        ref = S.launch(xd, T, K, P, torch.empty(B, dtype=torch.int32, device=dev),
+                       S.new_workspace(B, w.vocab, torch.float16, dev), uniforms=U)
         assert torch.equal(ref, o)
     del g
 
