@@ -316,6 +316,68 @@ def run_native(a):
         print(json.dumps(line), flush=True)
 
 
+def run_vocab_parallel(a):
+    """B=512, V=128256 bf16 split by vocabulary over the ranks; a
+    step = local candidates + NCCL all-gather + merge, the same ids on every
+    rank.  Time = max over ranks of CUDA-event time; value = rows/s of the job."""
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    from ecahlang_b200 import workloads as W
+    from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
+    w = W.config4(seed=0)
+    B, V = w.batch, w.vocab
+    off, loc = split_vocab(V, ws, rank)
+    bytes_in = B * loc * 2
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits[:, off:off + loc].contiguous().to(dev) for _ in range(nbuf)]
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    cap = min(256, 2048 // ws)
+    exch = None if ws > 1 else (lambda c, n, ac, an: (ac[0].copy_(c), an[0].copy_(n)))
+    smp = VocabParallelSampler(B, V, ws, rank, torch.bfloat16, dev, seed=77, cand_cap=cap, exchange=exch)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(a.warmup):
+        smp(bufs[i % nbuf], T, K, P)
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(a.steps):
+            smp(bufs[i % nbuf], T, K, P)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        ms_step = ms / a.steps
+        peak, peak_kind = _peaks()
+        alg = bytes_in   # per rank: its slice of the logits
+        achieved = alg / (ms_step / 1e3) / 1e9
+        print(json.dumps({
+            "metric": "vocab-parallel sampler rows/sec (configs[3]: B=512, V=128256 bf16, k=64, p=0.9)",
+            "value": B / (ms_step / 1e3), "unit": "rows/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c4_vocab_parallel B=512 V=128256 bf16", "slice_per_rank": loc,
+                       "cand_cap": cap, "exchange": "NCCL all_gather" if ws > 1 else "none (1 rank)",
+                       "launch": "eager (Python launch per step)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": a.steps * 2, "clocks": clk.summary(),
+        }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -323,10 +385,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["batch", "vp"], default="batch",
+                    help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     if a.impl == "reference":
         run_reference(a)
+    elif a.mode == "vp":
+        run_vocab_parallel(a)
     else:
         run_native(a)
 

@@ -22,7 +22,8 @@ STATUS = {0: "ok", 1: "null pointer", 2: "dtype", 3: "shape", 4: "workspace", 5:
 # exported symbols declared in include/ecah_sampler.h
 EXPORTS = ("ecah_sampler_abi_version", "ecah_status_string", "ecah_sampler_workspace_bytes",
            "ecah_sampler_launch", "ecah_hist_update", "ecah_philox_uniforms",
-           "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes")
+           "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes",
+           "ecah_vp_local", "ecah_vp_merge")
 
 
 class SamplerArgs(ctypes.Structure):
@@ -36,6 +37,22 @@ class SamplerArgs(ctypes.Structure):
         ("hist_mval", c_void_p), ("hist_cap", c_int32), ("num_slots", c_int32),
         ("flags", c_uint32),
         ("uniforms", c_void_p), ("philox_state", c_void_p), ("out", c_void_p), ("row_stats", c_void_p), ("probs_out", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
+class VPArgs(ctypes.Structure):
+    """Mirror of ``struct ecah_vp_args``."""
+    _fields_ = [
+        ("abi_version", c_int32), ("dtype", c_int32), ("batch", c_int32), ("vocab", c_int32),
+        ("vocab_offset", c_int32), ("vocab_local", c_int32), ("row_stride", c_int64),
+        ("logits", c_void_p), ("temperature", c_void_p), ("top_k", c_void_p), ("top_p", c_void_p),
+        ("rep_factor", c_void_p), ("row_slot", c_void_p), ("slot_len", c_void_p),
+        ("hist_tok", c_void_p), ("hist_cnt", c_void_p), ("hist_mval", c_void_p),
+        ("hist_cap", c_int32), ("num_slots", c_int32), ("cand_cap", c_int32),
+        ("cand", c_void_p), ("cand_count", c_void_p), ("world", c_int32),
+        ("all_cand", c_void_p), ("all_count", c_void_p), ("uniforms", c_void_p),
+        ("philox_state", c_void_p), ("out", c_void_p), ("row_stats", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
@@ -70,6 +87,10 @@ def lib():
         L.ecah_hist_update.argtypes = [c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
                                        c_void_p]
+        L.ecah_vp_local.restype = c_int32
+        L.ecah_vp_local.argtypes = [ctypes.POINTER(VPArgs), c_void_p]
+        L.ecah_vp_merge.restype = c_int32
+        L.ecah_vp_merge.argtypes = [ctypes.POINTER(VPArgs), c_void_p]
         L.ecah_philox_uniforms.restype = c_int32
         L.ecah_philox_uniforms.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_void_p]
         if L.ecah_sampler_abi_version() != ABI_VERSION:

@@ -1,0 +1,175 @@
+"""Vocab-parallel sampling: the LM-head logits of a row are split by vocabulary
+over `world` ranks (one process per GPU), each rank samples from its slice's
+candidates, and one all-gather of those candidates lets every rank draw the
+same token.
+
+ecahLang runs on a single GPU (ecahlang/env.py:112, main.py:201-204); this is
+the multi-GPU form of its sampling call (ecahlang/main.py:377-379) for a
+vocabulary-split LM head.  Per row, rank g writes every entry of its slice
+whose key is at or above the slice's k-th largest key (ties included), in
+vocab order with global ids (``ecah_vp_local``); since the row's k-th largest
+key is at least every slice's, the union holds the row's whole top-k set, and
+``ecah_vp_merge`` finishes the row exactly as the single-GPU sampler does.
+Rows need 1 <= top_k <= cand_cap (or T <= 0); other rows come back as -1.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Callable, Optional
+
+import torch
+
+from . import _abi
+from ._abi import VPArgs, check, lib
+from .sampler import PenaltyState, new_philox_state
+
+_DTYPES = {torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16}
+
+
+def split_vocab(vocab: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous slices: rank r holds [offset, offset + local); the first
+    vocab % world ranks hold one column more."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} not in [0, {world})")
+    base, extra = divmod(vocab, world)
+    offset = rank * base + min(rank, extra)
+    return offset, base + (1 if rank < extra else 0)
+
+
+def nccl_exchange(group=None) -> Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], None]:
+    """All-gather of the candidate lists and counts over a torch.distributed
+    group (NCCL over NVLink on GPUs), rank order."""
+    import torch.distributed as dist
+
+    def run(cand, count, all_cand, all_count):
+        dist.all_gather_into_tensor(all_cand.view(-1), cand.view(-1), group=group)
+        dist.all_gather_into_tensor(all_count.view(-1), count.view(-1), group=group)
+    return run
+
+
+class VocabParallelSampler:
+    """Per-rank state of the vocab-parallel sampler (buffers sized for
+    max_batch, Philox state seeded identically on every rank)."""
+
+    def __init__(self, max_batch: int, vocab: int, world: int, rank: int, dtype: torch.dtype,
+                 device="cuda", seed: int = 0, cand_cap: int = 256,
+                 exchange: Optional[Callable] = None):
+        if dtype not in _DTYPES:
+            raise RuntimeError(f"vocab-parallel sampling takes fp16/bf16 logits, not {dtype}")
+        if world * cand_cap > 2048:
+            raise ValueError("world * cand_cap must stay <= 2048")
+        self.vocab, self.world, self.rank, self.dtype = vocab, world, rank, dtype
+        self.offset, self.nlocal = split_vocab(vocab, world, rank)
+        self.cap = cand_cap
+        dev = torch.device(device)
+        self.device = dev
+        self.cand = torch.zeros(max_batch, cand_cap, dtype=torch.int64, device=dev)
+        self.count = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.all_cand = torch.zeros(world, max_batch, cand_cap, dtype=torch.int64, device=dev)
+        self.all_count = torch.zeros(world, max_batch, dtype=torch.int32, device=dev)
+        self.workspace = torch.zeros(256, dtype=torch.uint8, device=dev)
+        self.philox_state = new_philox_state(seed, 0, dev)
+        self.out = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.exchange = exchange if exchange is not None else nccl_exchange()
+
+    def _args(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats):
+        B = logits.shape[0]
+        a = VPArgs()
+        a.abi_version = _abi.ABI_VERSION
+        a.dtype = _DTYPES[logits.dtype]
+        a.batch, a.vocab = B, self.vocab
+        a.vocab_offset, a.vocab_local = self.offset, self.nlocal
+        a.row_stride = logits.stride(0)
+        a.logits = logits.data_ptr()
+        a.temperature, a.top_k, a.top_p = temperature.data_ptr(), top_k.data_ptr(), top_p.data_ptr()
+        if penalty is not None:
+            a.rep_factor = None if rep_factor is None else rep_factor.data_ptr()
+            a.row_slot = row_slot.data_ptr()
+            a.slot_len, a.hist_tok, a.hist_cnt = (penalty.slot_len.data_ptr(), penalty.tok.data_ptr(),
+                                                  penalty.cnt.data_ptr())
+            a.hist_mval = penalty.mval.data_ptr()
+            a.hist_cap, a.num_slots = penalty.capacity, penalty.num_slots
+        a.cand_cap = self.cap
+        a.cand, a.cand_count = self.cand.data_ptr(), self.count.data_ptr()
+        a.world = self.world
+        a.all_cand, a.all_count = self.all_cand.data_ptr(), self.all_count.data_ptr()
+        a.uniforms = None if uniforms is None else uniforms.data_ptr()
+        a.philox_state = self.philox_state.data_ptr()
+        a.out = self.out.data_ptr()
+        a.row_stats = None if row_stats is None else row_stats.data_ptr()
+        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        return a
+
+    def _check(self, logits, temperature, top_k, top_p, uniforms):
+        B = logits.shape[0]
+        if logits.shape[1] != self.nlocal:
+            raise RuntimeError(f"logits slice has {logits.shape[1]} columns, rank {self.rank} holds {self.nlocal}")
+        if logits.dtype not in _DTYPES:
+            raise RuntimeError(f"logits: fp16/bf16 expected, got {logits.dtype}")
+        if logits.device != self.device or logits.stride(1) != 1:
+            raise RuntimeError("logits slice must be on the sampler's device with unit column stride")
+        if B > self.cand.shape[0]:
+            raise RuntimeError(f"batch {B} exceeds max_batch {self.cand.shape[0]}")
+        for t, name, dt in ((temperature, "temperature", torch.float32), (top_k, "top_k", torch.int32),
+                            (top_p, "top_p", torch.float32)):
+            if t.dtype != dt or t.device != self.device or t.numel() != B or not t.is_contiguous():
+                raise RuntimeError(f"{name}: expected contiguous {dt} [{B}] on {self.device}")
+        if uniforms is not None and (uniforms.dtype != torch.float32 or uniforms.numel() != B
+                                     or uniforms.device != self.device):
+            raise RuntimeError("uniforms: expected float32 [B] on the sampler's device")
+
+    def local(self, logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+              penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
+              rep_factor: Optional[torch.Tensor] = None):
+        """This rank's candidate lists for the rows of `logits` ([B, vocab_local]):
+        returns views (cand [B, cap] int64, count [B] int32)."""
+        self._check(logits, temperature, top_k, top_p, None)
+        B = logits.shape[0]
+        a = self._args(logits, temperature.reshape(-1), top_k, top_p, None, penalty, row_slot, rep_factor, None)
+        check(lib().ecah_vp_local(ctypes.byref(a), torch.cuda.current_stream(self.device).cuda_stream),
+              "ecah_vp_local")
+        return self.cand[:B], self.count[:B]
+
+    def merge(self, all_cand: torch.Tensor, all_count: torch.Tensor, temperature: torch.Tensor,
+              top_k: torch.Tensor, top_p: torch.Tensor, uniforms: Optional[torch.Tensor] = None,
+              row_stats: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Draw from the gathered lists (all_cand [world, B, cap], all_count
+        [world, B], rank order).  Every rank gets the same [B] ids."""
+        B = all_count.shape[1]
+        if all_cand.shape != (self.world, B, self.cap) or all_cand.dtype != torch.int64 or not all_cand.is_contiguous():
+            raise RuntimeError(f"all_cand: expected contiguous int64 [{self.world}, {B}, {self.cap}]")
+        if all_count.shape != (self.world, B) or all_count.dtype != torch.int32 or not all_count.is_contiguous():
+            raise RuntimeError(f"all_count: expected contiguous int32 [{self.world}, {B}]")
+        a = VPArgs()
+        a.abi_version = _abi.ABI_VERSION
+        a.dtype = _DTYPES[self.dtype]
+        a.batch, a.vocab = B, self.vocab
+        a.vocab_offset, a.vocab_local, a.row_stride = self.offset, self.nlocal, self.nlocal
+        a.temperature, a.top_k, a.top_p = temperature.reshape(-1).data_ptr(), top_k.data_ptr(), top_p.data_ptr()
+        a.cand_cap, a.world = self.cap, self.world
+        a.all_cand, a.all_count = all_cand.data_ptr(), all_count.data_ptr()
+        a.uniforms = None if uniforms is None else uniforms.data_ptr()
+        a.philox_state = self.philox_state.data_ptr()
+        a.out = self.out.data_ptr()
+        a.row_stats = None if row_stats is None else row_stats.data_ptr()
+        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        check(lib().ecah_vp_merge(ctypes.byref(a), torch.cuda.current_stream(self.device).cuda_stream),
+              "ecah_vp_merge")
+        return self.out[:B]
+
+    def __call__(self, logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+                 top_p: torch.Tensor, uniforms: Optional[torch.Tensor] = None,
+                 penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
+                 rep_factor: Optional[torch.Tensor] = None, row_stats: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """logits: this rank's [B, vocab_local] slice.  Local candidates, the
+        exchange, then the merge; returns the [B] ids (identical on every rank)."""
+        self._check(logits, temperature, top_k, top_p, uniforms)
+        B = logits.shape[0]
+        cand, count = self.local(logits, temperature, top_k, top_p, penalty, row_slot, rep_factor)
+        if B == self.cand.shape[0]:
+            all_cand, all_count = self.all_cand, self.all_count
+        else:
+            all_cand = self.all_cand.view(-1)[: self.world * B * self.cap].view(self.world, B, self.cap)
+            all_count = self.all_count.view(-1)[: self.world * B].view(self.world, B)
+        self.exchange(cand, count, all_cand, all_count)
+        return self.merge(all_cand, all_count, temperature, top_k, top_p, uniforms, row_stats)

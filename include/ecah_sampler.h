@@ -161,6 +161,57 @@ ECAH_API int ecah_philox_uniforms(uint64_t* philox_state, int32_t batch, float* 
 ECAH_API int ecah_sampler_launch_noalloc(const ecah_sampler_args* args, void* stream);
 ECAH_API size_t ecah_sampler_noalloc_scratch_bytes(void);
 
+/*
+ * Vocab-parallel sampling (fp16/bf16 logits).  Each of `world` ranks holds
+ * columns [vocab_offset, vocab_offset + vocab_local) of the [batch, vocab]
+ * logits.  ecah_vp_local writes, per row, every local entry whose key is >=
+ * the slice's k-th largest key (ties included; k = top_k, 1 for greedy rows)
+ * in vocab order as (key << 32 | global id), at most cand_cap of them, and
+ * their count.  The caller all-gathers cand/cand_count over the ranks (rank
+ * order) into all_cand/all_count; ecah_vp_merge then draws the same token on
+ * every rank (the same uniforms / Philox state on every rank).  Rows need
+ * 1 <= top_k <= cand_cap (or T <= 0); rows with top-k off, or whose lists
+ * were truncated, get out = -1.  Replaces the whole-row FlashInfer call of
+ * ecahlang/main.py:377-379 when the LM head is split by vocabulary (ecahLang
+ * itself runs on one GPU, ecahlang/env.py:112).
+ */
+typedef struct ecah_vp_args {
+  int32_t abi_version;        /* = ECAH_SAMPLER_ABI_VERSION                      */
+  int32_t dtype;              /* ECAH_DTYPE_F16 or ECAH_DTYPE_BF16               */
+  int32_t batch;
+  int32_t vocab;              /* full vocabulary                                 */
+  int32_t vocab_offset;       /* this rank's first column                        */
+  int32_t vocab_local;        /* this rank's columns, 1 .. 65536                 */
+  int64_t row_stride;         /* elements between rows of the local slice        */
+  const void* logits;         /* [batch, row_stride] local slice                 */
+  const float* temperature;   /* [batch]                                         */
+  const int32_t* top_k;       /* [batch]                                         */
+  const float* top_p;         /* [batch]                                         */
+  const float* rep_factor;    /* as in ecah_sampler_args; history ids are global */
+  const int32_t* row_slot;
+  const int32_t* slot_len;
+  const int32_t* hist_tok;
+  const int32_t* hist_cnt;
+  const float* hist_mval;
+  int32_t hist_cap;
+  int32_t num_slots;
+  int32_t cand_cap;           /* candidates per row and rank, 1 .. 2048 / world  */
+  uint64_t* cand;             /* [batch, cand_cap] written by ecah_vp_local      */
+  int32_t* cand_count;        /* [batch] written by ecah_vp_local                */
+  int32_t world;              /* ranks, 1 .. 64                                  */
+  const uint64_t* all_cand;   /* [world, batch, cand_cap] gathered lists          */
+  const int32_t* all_count;   /* [world, batch] gathered counts                   */
+  const float* uniforms;      /* [batch], or NULL: Philox from philox_state       */
+  uint64_t* philox_state;     /* [2], advanced by 1 after the merge               */
+  int32_t* out;               /* [batch] sampled ids (the same on every rank)     */
+  float* row_stats;           /* [batch, 4] optional, as in ecah_sampler_args     */
+  void* workspace;            /* >= 256 bytes, zero-filled once                   */
+  size_t workspace_bytes;
+} ecah_vp_args;
+
+ECAH_API int ecah_vp_local(const ecah_vp_args* args, void* stream);
+ECAH_API int ecah_vp_merge(const ecah_vp_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,18 +39,19 @@ def test_abi_version_and_status_strings(L):
     assert L.ecah_sampler_workspace_bytes(128, 151936, 0) >= 4
 
 
-def test_struct_layout_matches_header(tmp_path):
+@pytest.mark.parametrize("mirror,cname", [(_abi.SamplerArgs, "ecah_sampler_args"), (_abi.VPArgs, "ecah_vp_args")])
+def test_struct_layout_matches_header(tmp_path, mirror, cname):
     """ctypes mirror vs offsetof() of the C struct, compiled with gcc."""
-    fields = [n for n, _ in _abi.SamplerArgs._fields_]
+    fields = [n for n, _ in mirror._fields_]
     src = tmp_path / "off.c"
     src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"ecah_sampler.h\"\nint main(){"
-                   + "".join(f'printf("%zu\\n", offsetof(ecah_sampler_args, {f}));' for f in fields)
-                   + 'printf("%zu\\n", sizeof(ecah_sampler_args));return 0;}')
+                   + "".join(f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields)
+                   + f'printf("%zu\\n", sizeof({cname}));return 0;}}')
     exe = tmp_path / "off"
     subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
                                           text=True).stdout.split()]
-    want = [getattr(_abi.SamplerArgs, f).offset for f in fields] + [ctypes.sizeof(_abi.SamplerArgs)]
+    want = [getattr(mirror, f).offset for f in fields] + [ctypes.sizeof(mirror)]
     assert got == want
 
 
@@ -80,6 +81,25 @@ def test_launch_rejects_bad_arguments_without_a_device(L):
     assert L.ecah_hist_update(None, 4, None, None, None, None, None, None, 8, 4, 0, None, None) == 1
     assert L.ecah_hist_update(None, 0, None, None, None, None, None, None, 8, 4, 0, None, None) == 0
     assert L.ecah_philox_uniforms(None, 4, None, 0, None) == 1
+
+
+def test_vocab_parallel_rejects_bad_arguments_without_a_device(L):
+    def vp(**kw):
+        a = _abi.VPArgs()
+        a.abi_version = _abi.ABI_VERSION
+        a.dtype, a.batch, a.vocab, a.vocab_offset, a.vocab_local, a.row_stride = 1, 4, 1000, 500, 500, 500
+        a.cand_cap, a.world = 64, 2
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return ctypes.byref(a)
+    assert L.ecah_vp_local(None, None) == 1
+    assert L.ecah_vp_local(vp(abi_version=3), None) == 6
+    assert L.ecah_vp_local(vp(dtype=2), None) == 2                  # fp32 logits: not supported
+    assert L.ecah_vp_local(vp(vocab_offset=600), None) == 3         # slice past the row end
+    assert L.ecah_vp_local(vp(vocab_local=70000, vocab=200000, row_stride=70000), None) == 3
+    assert L.ecah_vp_local(vp(world=16, cand_cap=256), None) == 3   # world * cap > 2048
+    assert L.ecah_vp_local(vp(), None) == 1                         # parameter arrays missing
+    assert L.ecah_vp_merge(vp(batch=0), None) == 0
 
 
 def test_product_path_fails_loudly_without_library(monkeypatch):
