@@ -4,18 +4,19 @@
 // talking to any other CTA.
 //
 // During the stream, per row mode (16-bit keys: fp16/bf16 logits):
-//   - every row: per-thread running (max key, lowest index holding it);
+//   - every row: per-thread running (max key, first round holding it);
 //   - rows with top-k (k <= kMaxN) or top-p: a candidate buffer in shared
 //     memory holding, in vocab order, every entry whose key is >= a running
-//     floor f.  f starts from a 256-bin histogram of the first round and is
-//     raised, when the buffer would overflow, to the N-th largest key of the
-//     buffer and the round's survivors (N = k, or kDenseN for top-p-only
-//     rows); the buffer always holds exactly the
-//     entries seen so far with key >= f, so every entry of the row at or above
-//     the final f is a candidate;
-//   - rows without top-k: softmax mass sum exp(z - q) per thread against a
-//     running per-thread reference q (online softmax), and for rows that draw
-//     from the whole distribution also per (round, warp) segment sums.
+//     floor f.  f starts at the N0-th largest key of the first round (N0 = k
+//     for top-k rows; for top-p-only rows kDenseN scaled to the round's share
+//     of the row) and is raised, when the buffer would overflow, to the N-th
+//     largest key of the buffer and the round's survivors; the buffer always
+//     holds exactly the entries seen so far with key >= f, so every entry of
+//     the row at or above the final f is a candidate;
+//   - rows without top-k: softmax masses per (round, warp) segment, each
+//     relative to the segment's own max z, so no mass overflows at any
+//     temperature; warps whose keys all lie 36 T below the first round's max
+//     skip them (their total mass is below 1e-9 of S).
 // After the stream the row max M, the thresholds (exact per-key counts of the
 // candidates, as in the cluster kernel's window path) and the draw (inverse
 // CDF over the candidates in vocab order, or over segment sums and then one
@@ -54,7 +55,8 @@ struct RSmem {
   unsigned lp[256 * 32];          // lane-private 256-bin histograms
   uint16_t ckey[kCB];             // candidates: key
   uint32_t cidx[kCB];             //             row index
-  float ss[kSegs];                // segment masses relative to a common reference
+  float ss[kSegs];                // segment masses relative to the segment's reference
+  float sq[kSegs];                //   and that reference (z of the segment's max)
   unsigned h256[256];
   unsigned red[2][kNW];           // reduction scratch, alternating
   int wcnt[2][kNW];
@@ -150,20 +152,30 @@ __device__ __forceinline__ float rscan_f(float v, RSmem& S, int& ph, float* tota
 // Round r of `row`: entries [r * kRound, ...) of the row, n of them valid.
 __device__ __forceinline__ int round_len(int V, int r) { return min(kRound, V - r * kRound); }
 
-__device__ __forceinline__ void issue_round(const KParams& P, uint4* st, int row, int r) {
+// cp.async of round r's whole 16-byte chunks, in row order: thread t copies
+// chunks t and t + 1024.  (Placing a lane pair's chunks in two halves of the
+// stage makes the shared loads below conflict-free, but measured slower on
+// the copy side.)  row4: the row's first chunk.
+__device__ __forceinline__ void issue_round(const KParams& P, uint4* st, const uint4* row4, int r) {
   if (!P.vec_ok) return;
-  const int n = round_len(P.V, r);
-  const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
-                                                   static_cast<long long>(row) * P.row_stride +
-                                                   static_cast<long long>(r) * kRound);
-  const int nfull = n >> 3;
-  for (int v = threadIdx.x; v < nfull; v += kT) cp_async16(st + v, s4 + v);
+  const int nfull = round_len(P.V, r) >> 3;
+  const uint4* s4 = row4 + static_cast<long long>(r) * kRVecs;
+  const int c0 = threadIdx.x, c1 = threadIdx.x + kT;
+  if (c0 < nfull) cp_async16(st + c0, s4 + c0);
+  if (c1 < nfull) cp_async16(st + c1, s4 + c1);
+}
+
+// Whether the row has a repetition-penalty history to patch in.
+__device__ __forceinline__ bool row_has_penalty(const KParams& P, int row) {
+  if (!P.row_slot) return false;
+  const int slot = P.row_slot[row];
+  return slot >= 0 && slot < P.num_slots && min(P.slot_len[slot], P.hist_cap) > 0;
 }
 
 // Ragged tail / unaligned rows with plain loads, padding (key 0), penalty
 // patch.  Returns with the stage complete for every thread.
 template <int DT>
-__device__ void complete_round(const KParams& P, uint4* st, int row, int r) {
+__device__ void complete_round(const KParams& P, uint4* st, int row, int r, bool pen) {
   using Dt = DType<DT>;
   const int tid = threadIdx.x;
   const int n = round_len(P.V, r);
@@ -171,28 +183,25 @@ __device__ void complete_round(const KParams& P, uint4* st, int row, int r) {
   const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
   uint16_t* raw = reinterpret_cast<uint16_t*>(st);
   const int done = P.vec_ok ? ((n >> 3) << 3) : 0;
-  const bool tail = done < kRound;
-  if (tail) {
+  if (done < kRound) {
     for (int i = done + tid; i < kRound; i += kT) raw[i] = (i < n) ? src[i] : static_cast<uint16_t>(0xFFFFu);
     __syncthreads();
   }
-  if (P.row_slot) {
+  if (pen) {
     const int slot = P.row_slot[row];
-    if (slot >= 0 && slot < P.num_slots) {
-      const int len = min(P.slot_len[slot], P.hist_cap);
-      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
-      const long long base = static_cast<long long>(slot) * P.hist_cap;
-      for (int h = tid; h < len; h += kT) {
-        const int tok = P.hist_tok[base + h];
-        const int cnt = P.hist_cnt[base + h];
-        const int li = tok - c0;
-        if (cnt <= 0 || li < 0 || li >= n) continue;
-        const float x = Dt::to_f32(raw[li]);
-        const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
-        raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
-      }
-      __syncthreads();
+    const int len = min(P.slot_len[slot], P.hist_cap);
+    const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+    const long long base = static_cast<long long>(slot) * P.hist_cap;
+    for (int h = tid; h < len; h += kT) {
+      const int tok = P.hist_tok[base + h];
+      const int cnt = P.hist_cnt[base + h];
+      const int li = tok - c0;
+      if (cnt <= 0 || li < 0 || li >= n) continue;
+      const float x = Dt::to_f32(raw[li]);
+      const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
+      raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
     }
+    __syncthreads();
   }
 }
 
@@ -267,15 +276,23 @@ __device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
   }
 }
 
-// Streams the whole row through the pipeline and calls fn(r, raw, w, nv)
-// once per round with the thread's raw words and keys (nv of its 16 entries
-// are in the row; the rest are padding, key 0); fn may use barriers (every
-// thread calls it).  The next rounds are already in flight while fn runs.
+// Streams the whole row through the pipeline and calls fn(r, st, raw, w, nv)
+// once per round with the round's stage and the thread's raw words and keys
+// (nv of its 16 entries are in the row; the rest are padding, key 0); fn may
+// use barriers (every thread calls it).  The next rounds are already in
+// flight while fn runs; the stage stays intact until fn returns.  (A single
+// bulk copy per round on the TMA engine, completing on an mbarrier, measured
+// about 2 % slower than these per-thread copies.)
 template <int DT, typename Fn>
 __device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
   const int R = (P.V + kRound - 1) / kRound;
+  const bool pen = row_has_penalty(P, row);
+  const uint16_t* rowp = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
+  // rounds that need completing: all (unaligned rows, penalties), else a ragged last one
+  const int rc = (!P.vec_ok || pen) ? 0 : ((P.V % kRound) ? R - 1 : R);
+  const uint4* row4 = reinterpret_cast<const uint4*>(rowp);
   for (int s = 0; s < kStages - 1; ++s) {
-    if (s < R) issue_round(P, S.stage[s], row, s);
+    if (s < R) issue_round(P, S.stage[s], row4, s);
     cp_async_commit();
   }
   for (int r = 0; r < R; ++r) {
@@ -284,14 +301,14 @@ __device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
     // r - 1, whose stage the next copy reuses
     __syncthreads();
     const int nx = r + kStages - 1;
-    if (nx < R) issue_round(P, S.stage[nx % kStages], row, nx);
+    if (nx < R) issue_round(P, S.stage[nx % kStages], row4, nx);
     cp_async_commit();
     uint4* st = S.stage[r % kStages];
-    complete_round<DT>(P, st, row, r);
+    if (r >= rc) complete_round<DT>(P, st, row, r, pen);
     uint32_t raw[8], w[8];
     round_load(st, raw, w);
-    const int nv = max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
-    fn(r, raw, w, nv);
+    const int nv = (r < R - 1) ? kEPT : max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
+    fn(r, static_cast<const uint4*>(st), raw, w, nv);
   }
   cp_async_wait_group<0>();
   __syncthreads();
@@ -467,6 +484,14 @@ __device__ __forceinline__ float emass(float y, float T, float rT, float q, bool
   return t1 ? ex2_approx(__fmul_rn(__fsub_rn(y, q), kLog2e)) : mass_of(y, T, rT, q);
 }
 
+// segment s's mass rescaled to M (0 past nseg, for empty segments and for
+// references far enough below M to underflow)
+__device__ __forceinline__ float seg_mass(const RSmem& S, int s, int nseg, float M) {
+  if (s >= nseg) return 0.f;
+  const float ss = S.ss[s];
+  return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmul_rn(__fsub_rn(S.sq[s], M), kLog2e))) : 0.f;
+}
+
 // ------------------------------------------------------------ the kernel
 template <int DT>
 __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
@@ -494,52 +519,78 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     // running state
     unsigned best = 0u;       // thread max key
     int bround = 0;           // first round where this thread met it
-    float q0 = 0.f;           // row mass reference: z of the first round's max
-    float sacc = 0.f;         // thread mass relative to q0
     unsigned f = 0u;          // candidate floor
     int fill = 0;
     bool overflow = (N == 0);
 
-    stream_row<DT>(P, S, row, [&](int r, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
-      uint32_t m2 = w[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) m2 = max16x2(m2, w[j]);
+    uint32_t kcut = 0u;       // mass rows: warps whose keys all lie below skip their masses
+    const uint32_t kinf = C::from_val(INFINITY), kninf = C::from_val(-INFINITY);
+
+    stream_row<DT>(P, S, row, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+      const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
+                                  max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
       const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);  // padding keys are 0
       if (tm > best) { best = tm; bround = r; }
       uint32_t k0 = 0u;  // round-0 max (round 0 only)
       if (r == 0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
 
       if (mass_all) {
-        if (r == 0) q0 = __fdiv_rn(C::value(k0), T);
-        // NaN masses (padding, NaN logits) drop out through fmaxf
-        float rs = 0.f;
-        if (t1) {
-          const float nq = -q0;
+        if (r == 0) {
+          // entries with y below y0 - 36 T have mass below e^-36 relative to
+          // the row max; all of them together stay below V e^-36 < 1e-9 of S
+          const float ylo = __fsub_rn(C::value(k0), __fmul_rn(36.0f, T));
+          kcut = (ylo > -INFINITY) ? C::from_val(ylo) : 0u;
+        }
+        // Segment (round, warp) masses relative to the segment's own max z,
+        // so no mass overflows whatever M turns out to be; NaN masses
+        // (padding, NaN logits) drop out through fmaxf.
+        float rs = 0.f, qw = -INFINITY;
+        if (__any_sync(0xFFFFFFFFu, tm >= kcut)) {
+          uint32_t tr = tm;
+          if (tm > kinf) {
+            // NaN keys lie above +inf: the reference is the max of the others
+            tr = 0u;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float2 y = vals2<DT>(raw[j]);
-            rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.x, nq), kLog2e)), 0.f);
-            rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.y, nq), kLog2e)), 0.f);
+            for (int j = 0; j < kEPT; ++j) {
+              const uint32_t key = ECAH_RKEY(w, j);
+              if (key <= kinf) tr = max(tr, key);
+            }
           }
-        } else {
+          const uint32_t kw = __reduce_max_sync(0xFFFFFFFFu, tr);
+          if (kw > kninf) {
+            const float yw = C::value(kw);
+            qw = t1 ? yw : __fdiv_rn(yw, T);
+            if (t1) {
+              const float nq = -qw;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float2 y = vals2<DT>(raw[j]);
-            rs += fmaxf(mass_of(y.x, T, rT, q0), 0.f);
-            rs += fmaxf(mass_of(y.y, T, rT, q0), 0.f);
+              for (int j = 0; j < 8; ++j) {
+                const float2 y = vals2<DT>(raw[j]);
+                rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.x, nq), kLog2e)), 0.f);
+                rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.y, nq), kLog2e)), 0.f);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float2 y = vals2<DT>(raw[j]);
+                rs += fmaxf(mass_of(y.x, T, rT, qw), 0.f);
+                rs += fmaxf(mass_of(y.y, T, rT, qw), 0.f);
+              }
+            }
           }
         }
-        sacc += rs;
-        if (segs) {
-          const float ws = warp_sum(rs);
-          if (lane == 0) S.ss[r * kNW + warp] = ws;
-        }
+        const float ws = warp_sum(rs);
+        if (lane == 0) { S.ss[r * kNW + warp] = ws; S.sq[r * kNW + warp] = qw; }
       }
 
       if (!overflow) {
         if (r == 0) {
-          // first floor: counts of the 4096 keys below the round's max k0 in
-          // 256 bins of 16; the lowest key of the bin where N is reached
+          // First floor: the N0-th largest key of round 0, from counts of the
+          // 4096 keys below the round's max k0 in 256 bins of 16 (the lowest
+          // key of the bin where N0 is reached).  Top-k rows take N0 = k (the
+          // row's k-th largest key is never below it); top-p rows scale N to
+          // the round's share of the row, so about N entries pass in all.
+          const int n0 = round_len(P.V, 0);
+          const int N0 = topk ? N : max(1, static_cast<int>((static_cast<long long>(N) * n0 + P.V - 1) / P.V));
           lp_zero(S);
 #pragma unroll
           for (int j = 0; j < kEPT; ++j) {
@@ -549,22 +600,23 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           }
           lp_reduce(S);
           unsigned above;
-          const int b = h256_select_asc(S, static_cast<unsigned>(N), &above);
+          const int b = h256_select_asc(S, static_cast<unsigned>(N0), &above);
           const uint32_t d = (b >= 0) ? static_cast<uint32_t>(b) * 16u + 15u : 4095u;
           f = (k0 > d) ? max(k0 - d, 1u) : 1u;  // key 0 is padding
         }
-        // survivors (key >= f >= 1; padding keys are 0 and never survive)
-        auto count = [&](unsigned fl) -> int {
-          if (!__any_sync(0xFFFFFFFFu, tm >= fl)) return 0;
+        // survivor bits (key >= f >= 1; padding keys are 0 and never
+        // survive): bit q = entry 2q, bit 16 + q = entry 2q + 1
+        auto survivors = [&](unsigned fl) -> uint32_t {
+          if (!__any_sync(0xFFFFFFFFu, tm >= fl)) return 0u;
           const uint32_t fm2 = (fl - 1u) * 0x00010001u;
-          uint32_t acc = 0u;
+          uint32_t sb = 0u;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) acc += surv2(w[q], fm2);
-          return static_cast<int>((acc & 0xFFFFu) + (acc >> 16));
+          for (int q = 0; q < 8; ++q) sb |= surv2(w[q], fm2) << q;
+          return sb;
         };
-        int cnt = count(f);
+        uint32_t sb = survivors(f);
         int total;
-        int off = rscan_i(cnt, S, ph, &total);
+        int off = rscan_i(__popc(sb), S, ph, &total);
         if (fill + total > kCB) {
           // raise the floor toward the N-th largest key of the buffer and this
           // round's survivors, drop what falls below
@@ -573,29 +625,27 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
             f = nf;
             fill = cand_compact(S, fill, f, ph);
           }
-          cnt = count(f);
-          off = rscan_i(cnt, S, ph, &total);
+          sb = survivors(f);
+          off = rscan_i(__popc(sb), S, ph, &total);
           if (fill + total > kCB) overflow = true;
         }
         if (!overflow) {
-          if (__any_sync(0xFFFFFFFFu, cnt > 0)) {
-            const uint32_t fm2 = (f - 1u) * 0x00010001u;
-            const uint32_t base = static_cast<uint32_t>(r * kRound + kEPT * tid);
-            int o = fill + off;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint32_t fl = surv2(w[q], fm2);
-              if (fl & 1u) {
-                S.ckey[o] = static_cast<uint16_t>(w[q] & 0xFFFFu);
-                S.cidx[o] = base + 2u * q;
-                ++o;
-              }
-              if (fl >> 16) {
-                S.ckey[o] = static_cast<uint16_t>(w[q] >> 16);
-                S.cidx[o] = base + 2u * q + 1u;
-                ++o;
-              }
-            }
+          // append in vocab order: a survivor's slot is the thread's offset
+          // plus the survivors among its lower entries; its key is re-read
+          // from the stage
+          const uint16_t* sr = reinterpret_cast<const uint16_t*>(st);
+          const uint32_t base = static_cast<uint32_t>(r * kRound + kEPT * tid);
+          const int o = fill + off;
+          uint32_t m = sb;
+          while (m) {
+            const int bit = __ffs(m) - 1;
+            m &= m - 1u;
+            const int q = bit & 15, h = bit >> 4;
+            const int e = 2 * q + h;
+            const uint32_t lower = (((1u << q) - 1u) * 0x00010001u) | (static_cast<uint32_t>(h) << q);
+            const int pos = o + __popc(sb & lower);
+            S.ckey[pos] = static_cast<uint16_t>(key16(sr[kEPT * tid + e]));
+            S.cidx[pos] = base + static_cast<uint32_t>(e);
           }
           fill += total;
         }
@@ -640,11 +690,9 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       float S_all = 0.f;
       bool mass_ok = true;
       if (mass_all) {
-        // masses were taken relative to q0 <= M: fine unless M - q0 overflows them
-        mass_ok = isfinite(q0) && __fsub_rn(M, q0) < 80.0f;
-        const float s0 = rsum_f(sacc, S, ph);
-        S_all = mass_ok ? __fmul_rn(s0, ex2_approx(__fmul_rn(__fsub_rn(q0, M), kLog2e))) : 0.f;
-        mass_ok = mass_ok && isfinite(S_all);
+        // segment masses were taken relative to references <= M
+        S_all = rsum_f(seg_mass(S, tid, R * kNW, M), S, ph);
+        mass_ok = isfinite(S_all);
       }
       bool fast = (!overflow || segs) && mass_ok;
       uint32_t key_lo_k = 0u, key_lo = 0u;
@@ -747,7 +795,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         key_lo_k = 0u;
         if (topk) {
           lp_zero(S);
-          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j)
               if (j < nv) atomicAdd(&S.lp[((ECAH_RKEY(w, j) >> 8) << 5) | static_cast<uint32_t>(lane)], 1u);
@@ -756,7 +804,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           unsigned above;
           const int hb = h256_select_desc(S, static_cast<unsigned>(k_eff), &above);
           lp_zero(S);
-          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -775,7 +823,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const uint32_t klo = max(key_lo_k, key_cut);
           lp_zero(S);
           float sk = 0.f;
-          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -806,7 +854,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const int hb = S.ib[2];
           lp_zero(S);
           float above = 0.f;
-          stream_row<DT>(P, S, row, [&](int, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -874,9 +922,8 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       } else {
         // segment sums: from the stream (whole distribution) or a re-stream
         const int nseg = R * kNW;
-        float sref = q0;  // reference of the segment sums
         if (!(fast && segs)) {
-          stream_row<DT>(P, S, row, [&](int r, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
             float a = 0.f;
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
@@ -884,17 +931,11 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
               if (j < nv && key >= kdraw) a += mass_of(C::value(key), T, rT, M);
             }
             a = warp_sum(a);
-            if (lane == 0) S.ss[r * kNW + warp] = a;
+            if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = M; }
           });
-          sref = M;
         }
         // per-segment mass relative to M, then the segment holding u * Z
-        const float sc = ex2_approx(__fmul_rn(__fsub_rn(sref, M), kLog2e));
-        float v = 0.f;
-        if (tid < nseg) {
-          const float ss = S.ss[tid];
-          v = (ss > 0.f) ? __fmul_rn(ss, sc) : 0.f;
-        }
+        const float v = seg_mass(S, tid, nseg, M);
         const float ex = rscan_f(v, S, ph, &Z);
         const float target = __fmul_rn(u, Z);
         const int mine = (tid < nseg && v > 0.f && ex + v > target) ? tid : INT_MAX;
