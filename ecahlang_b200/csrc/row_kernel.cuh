@@ -56,7 +56,7 @@ struct RSmem {
   uint16_t ckey[kCB];             // candidates: key
   uint32_t cidx[kCB];             //             row index
   float ss[kSegs];                // segment masses relative to the segment's reference
-  float sq[kSegs];                //   and that reference (z of the segment's max)
+  float sq[kSegs];                //   and that reference (z of the segment's max, times log2 e)
   unsigned h256[256];
   unsigned red[2][kNW];           // reduction scratch, alternating
   int wcnt[2][kNW];
@@ -98,26 +98,24 @@ __device__ __forceinline__ float rsum_f(float v, RSmem& S, int& ph) {
   return t;
 }
 
-// exclusive prefix of v over threads in thread order; *total = sum
+// exclusive prefix of v over threads in thread order; *total = sum.  Warps
+// whose v are all 0 skip the lane scan; the prefix over warps and the total
+// are two warp reductions of the per-warp sums.
 __device__ __forceinline__ int rscan_i(int v, RSmem& S, int& ph, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = v;
+  if (__any_sync(0xFFFFFFFFu, v != 0)) {
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += y;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
   }
   if (lane == 31) S.wcnt[ph][warp] = incl;
   __syncthreads();
   const int wv = S.wcnt[ph][lane];
-  int winc = wv;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xFFFFFFFFu, winc, o);
-    if (lane >= o) winc += y;
-  }
-  const int base = __shfl_sync(0xFFFFFFFFu, winc - wv, warp);
-  *total = __shfl_sync(0xFFFFFFFFu, winc, 31);
+  const int base = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(lane < warp ? wv : 0)));
+  *total = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(wv)));
   ph ^= 1;
   return base + incl - v;
 }
@@ -152,17 +150,30 @@ __device__ __forceinline__ float rscan_f(float v, RSmem& S, int& ph, float* tota
 // Round r of `row`: entries [r * kRound, ...) of the row, n of them valid.
 __device__ __forceinline__ int round_len(int V, int r) { return min(kRound, V - r * kRound); }
 
-// cp.async of round r's whole 16-byte chunks, in row order: thread t copies
-// chunks t and t + 1024.  (Placing a lane pair's chunks in two halves of the
-// stage makes the shared loads below conflict-free, but measured slower on
-// the copy side.)  row4: the row's first chunk.
-__device__ __forceinline__ void issue_round(const KParams& P, uint4* st, const uint4* row4, int r) {
+// Per-warp streaming: warp w owns entries [r * kRound + 512 w, + 512) of
+// every round r (lane l: 16 l .. 16 l + 15 of them) and four private 1 KB
+// stages; it waits only for its own copies, so warps never wait on one
+// another while the row streams.
+constexpr int kWS = kRound / kNW;         // entries of a warp slice (512)
+constexpr int kWV = kWS / 8;              // 16-byte chunks of a slice (64)
+
+// this warp's stage s
+__device__ __forceinline__ uint4* wstage(RSmem& S, int s) {
+  return &S.stage[0][0] + ((threadIdx.x >> 5) * kStages + s) * kWV;
+}
+
+// first row entry of this warp's slice of round r, and how many lie in the row
+__device__ __forceinline__ int slice_e0(int r) { return r * kRound + (threadIdx.x >> 5) * kWS; }
+__device__ __forceinline__ int slice_len(int V, int r) { return max(0, min(kWS, V - slice_e0(r))); }
+
+// cp.async of the slice's whole 16-byte chunks: lane l copies chunks l and l + 32
+__device__ __forceinline__ void issue_slice(const KParams& P, uint4* st, const uint4* row4, int r) {
   if (!P.vec_ok) return;
-  const int nfull = round_len(P.V, r) >> 3;
-  const uint4* s4 = row4 + static_cast<long long>(r) * kRVecs;
-  const int c0 = threadIdx.x, c1 = threadIdx.x + kT;
-  if (c0 < nfull) cp_async16(st + c0, s4 + c0);
-  if (c1 < nfull) cp_async16(st + c1, s4 + c1);
+  const int nfull = slice_len(P.V, r) >> 3;
+  const uint4* s4 = row4 + (slice_e0(r) >> 3);
+  const int lane = threadIdx.x & 31;
+  if (lane < nfull) cp_async16(st + lane, s4 + lane);
+  if (lane + 32 < nfull) cp_async16(st + lane + 32, s4 + lane + 32);
 }
 
 // Whether the row has a repetition-penalty history to patch in.
@@ -173,35 +184,34 @@ __device__ __forceinline__ bool row_has_penalty(const KParams& P, int row) {
 }
 
 // Ragged tail / unaligned rows with plain loads, padding (key 0), penalty
-// patch.  Returns with the stage complete for every thread.
+// patch, for this warp's slice.  Returns with the slice complete for the warp.
 template <int DT>
-__device__ void complete_round(const KParams& P, uint4* st, int row, int r, bool pen) {
+__device__ void complete_slice(const KParams& P, uint4* st, int row, int r, bool pen) {
   using Dt = DType<DT>;
-  const int tid = threadIdx.x;
-  const int n = round_len(P.V, r);
-  const int c0 = r * kRound;
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
+  const int lane = threadIdx.x & 31;
+  const int n = slice_len(P.V, r);
+  const int e0 = slice_e0(r);
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + e0;
   uint16_t* raw = reinterpret_cast<uint16_t*>(st);
   const int done = P.vec_ok ? ((n >> 3) << 3) : 0;
-  if (done < kRound) {
-    for (int i = done + tid; i < kRound; i += kT) raw[i] = (i < n) ? src[i] : static_cast<uint16_t>(0xFFFFu);
-    __syncthreads();
+  if (done < kWS) {
+    for (int i = done + lane; i < kWS; i += 32) raw[i] = (i < n) ? src[i] : static_cast<uint16_t>(0xFFFFu);
+    __syncwarp();
   }
   if (pen) {
     const int slot = P.row_slot[row];
     const int len = min(P.slot_len[slot], P.hist_cap);
     const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
     const long long base = static_cast<long long>(slot) * P.hist_cap;
-    for (int h = tid; h < len; h += kT) {
-      const int tok = P.hist_tok[base + h];
+    for (int h = lane; h < len; h += 32) {
+      const int li = P.hist_tok[base + h] - e0;
       const int cnt = P.hist_cnt[base + h];
-      const int li = tok - c0;
       if (cnt <= 0 || li < 0 || li >= n) continue;
       const float x = Dt::to_f32(raw[li]);
       const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
       raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
     }
-    __syncthreads();
+    __syncwarp();
   }
 }
 
@@ -241,9 +251,11 @@ template <> __device__ __forceinline__ float2 vals2<ECAH_DTYPE_BF16>(uint32_t w)
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-// this thread's 16 raw logits (entries 16*tid .. 16*tid+15 of the round) and keys
+// this thread's 16 raw logits (entries 16 lane .. 16 lane + 15 of its warp's
+// slice) and keys
 __device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8]) {
-  const uint4 a = st[2 * threadIdx.x], b = st[2 * threadIdx.x + 1];
+  const int lane = threadIdx.x & 31;
+  const uint4 a = st[2 * lane], b = st[2 * lane + 1];
   raw[0] = a.x; raw[1] = a.y; raw[2] = a.z; raw[3] = a.w;
   raw[4] = b.x; raw[5] = b.y; raw[6] = b.z; raw[7] = b.w;
 #pragma unroll
@@ -276,37 +288,38 @@ __device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
   }
 }
 
-// Streams the whole row through the pipeline and calls fn(r, st, raw, w, nv)
-// once per round with the round's stage and the thread's raw words and keys
-// (nv of its 16 entries are in the row; the rest are padding, key 0); fn may
-// use barriers (every thread calls it).  The next rounds are already in
-// flight while fn runs; the stage stays intact until fn returns.  (A single
-// bulk copy per round on the TMA engine, completing on an mbarrier, measured
-// about 2 % slower than these per-thread copies.)
+// Streams the whole row through the per-warp pipelines and calls
+// fn(r, st, raw, w, nv) once per round with the warp's stage (its slice) and
+// the thread's raw words and keys (nv of its 16 entries are in the row; the
+// rest are padding, key 0).  Warps run through the rounds independently: fn
+// may use block barriers only where every warp reaches them in the same
+// round.  The next rounds are in flight while fn runs; the stage stays intact
+// until fn returns.  Ends with a block barrier.
 template <int DT, typename Fn>
 __device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
   const int R = (P.V + kRound - 1) / kRound;
   const bool pen = row_has_penalty(P, row);
-  const uint16_t* rowp = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
+  const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
+                                                     static_cast<long long>(row) * P.row_stride);
   // rounds that need completing: all (unaligned rows, penalties), else a ragged last one
   const int rc = (!P.vec_ok || pen) ? 0 : ((P.V % kRound) ? R - 1 : R);
-  const uint4* row4 = reinterpret_cast<const uint4*>(rowp);
+  __syncthreads();  // the stages may have served as finishing scratch
   for (int s = 0; s < kStages - 1; ++s) {
-    if (s < R) issue_round(P, S.stage[s], row4, s);
+    if (s < R) issue_slice(P, wstage(S, s), row4, s);
     cp_async_commit();
   }
   for (int r = 0; r < R; ++r) {
     cp_async_wait_group<kStages - 2>();
-    // round r landed for every thread, and every thread is done with round
-    // r - 1, whose stage the next copy reuses
-    __syncthreads();
-    const int nx = r + kStages - 1;
-    if (nx < R) issue_round(P, S.stage[nx % kStages], row4, nx);
-    cp_async_commit();
-    uint4* st = S.stage[r % kStages];
-    if (r >= rc) complete_round<DT>(P, st, row, r, pen);
+    // the slice of round r landed for the warp, and the warp is done with
+    // round r - 1, whose stage the next copy reuses
+    __syncwarp();
+    uint4* st = wstage(S, r % kStages);
+    if (r >= rc) complete_slice<DT>(P, st, row, r, pen);
     uint32_t raw[8], w[8];
     round_load(st, raw, w);
+    const int nx = r + kStages - 1;
+    if (nx < R) issue_slice(P, wstage(S, nx % kStages), row4, nx);
+    cp_async_commit();
     const int nv = (r < R - 1) ? kEPT : max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
     fn(r, static_cast<const uint4*>(st), raw, w, nv);
   }
@@ -408,88 +421,236 @@ __device__ __forceinline__ int h256_select_asc(RSmem& S, unsigned n, unsigned* a
   return S.ib[14];
 }
 
-// N-th largest key among the candidate buffer [0, fill) and this round's
-// entries with key >= f (N <= their number); kref >= every one of those keys.
-// Bins are measured down from kref, so the counted keys spread over many:
-// 256 bins of 2^s keys give the lowest key of the bin where N is reached (a
-// floor keeping at least N); only when that floor would not rise above f are
-// the 2^s keys of the bin counted one by one for the exact N-th largest.
-__device__ unsigned cand_nth(RSmem& S, int fill, const uint32_t (&w)[8], int nv, unsigned f, unsigned kref,
-                             unsigned N) {
-  const uint32_t lane = threadIdx.x & 31;
+// ------------------------------------------------------- per-warp candidates
+// Warp w keeps its candidates in region [w kCBW, (w + 1) kCBW) of the buffer,
+// in vocab order; after the stream the regions are gathered into one buffer
+// in vocab order.
+constexpr int kCBW = kCB / kNW;           // 256
+constexpr int kKeepW = kCBW / 2;          // a compaction keeps about this many
+
+// Among bins 0..255 (ascending, 8 per lane) of the warp-private histogram h,
+// the first whose running count reaches n; -1 if the total stays below n.
+// *above = count of the bins before it.  Warp-uniform result.
+__device__ __forceinline__ int warp_sel_asc(const unsigned* h, unsigned n, unsigned* above) {
+  const int lane = threadIdx.x & 31;
+  unsigned v[8], s = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { v[j] = h[lane * 8 + j]; s += v[j]; }
+  unsigned incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= n);
+  if (!hit) { *above = __shfl_sync(0xFFFFFFFFu, incl, 31); return -1; }
+  const int L = __ffs(hit) - 1;
+  int bin = 0;
+  unsigned ab = 0u;
+  if (lane == L) {
+    unsigned acc = incl - s;
+    bin = -1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (bin < 0 && acc + v[j] >= n) { bin = lane * 8 + j; ab = acc; }
+      acc += v[j];
+    }
+  }
+  bin = __shfl_sync(0xFFFFFFFFu, bin, L);
+  *above = __shfl_sync(0xFFFFFFFFu, ab, L);
+  return bin;
+}
+
+// N-th largest key among the warp's region [0, fill) and this round's entries
+// with key >= f (N <= their number); kref >= every one of those keys.  Bins
+// are measured down from kref: 256 bins of 2^s keys give the lowest key of
+// the bin where N is reached (a floor keeping at least N); only when that
+// floor would not rise above f are the 2^s keys of the bin counted one by one.
+__device__ unsigned wcand_nth(RSmem& S, int fill, const uint32_t (&w)[8], int nv, unsigned f, unsigned kref,
+                              unsigned N) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned* h = S.lp + warp * 256;
+  const uint16_t* ck = S.ckey + warp * kCBW;
   int sh = 0;
   while (((kref - f) >> sh) >= 256u) ++sh;
-  lp_zero(S);
-  for (int i = threadIdx.x; i < fill; i += kT) atomicAdd(&S.lp[(((kref - S.ckey[i]) >> sh) << 5) | lane], 1u);
+  for (int i = lane; i < 256; i += 32) h[i] = 0u;
+  __syncwarp();
+  for (int i = lane; i < fill; i += 32) {
+    const unsigned key = ck[i];
+    if (key >= f) atomicAdd(&h[(kref - key) >> sh], 1u);
+  }
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) {
     const uint32_t key = ECAH_RKEY(w, j);
-    if (j < nv && key >= f) atomicAdd(&S.lp[(((kref - key) >> sh) << 5) | lane], 1u);
+    if (j < nv && key >= f) atomicAdd(&h[(kref - key) >> sh], 1u);
   }
-  lp_reduce(S);
+  __syncwarp();
   unsigned above;
-  const int b1 = h256_select_asc(S, N, &above);
+  const int b1 = warp_sel_asc(h, N, &above);
+  __syncwarp();
   if (sh == 0 || b1 < 0) return kref - static_cast<unsigned>(max(b1, 0));
   // the lowest key of bin b1 keeps at least N (and the whole bin) when it lies above f
-  const unsigned lowest = kref - ((static_cast<unsigned>(b1) << sh) + ((1u << sh) - 1u));
-  if (kref >= ((static_cast<unsigned>(b1) << sh) + ((1u << sh) - 1u)) && lowest > f) return lowest;
+  const unsigned span = (static_cast<unsigned>(b1) << sh) + ((1u << sh) - 1u);
+  if (kref >= span && kref - span > f) return kref - span;
   const unsigned msk = (1u << sh) - 1u;
-  lp_zero(S);
-  for (int i = threadIdx.x; i < fill; i += kT) {
-    const unsigned d = kref - S.ckey[i];
-    if (static_cast<int>(d >> sh) == b1) atomicAdd(&S.lp[((d & msk) << 5) | lane], 1u);
+  for (int i = lane; i < 256; i += 32) h[i] = 0u;
+  __syncwarp();
+  for (int i = lane; i < fill; i += 32) {
+    const unsigned d = kref - ck[i];
+    if (ck[i] >= f && static_cast<int>(d >> sh) == b1) atomicAdd(&h[d & msk], 1u);
   }
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) {
     const uint32_t key = ECAH_RKEY(w, j);
     const unsigned d = kref - key;
-    if (j < nv && key >= f && static_cast<int>(d >> sh) == b1) atomicAdd(&S.lp[((d & msk) << 5) | lane], 1u);
+    if (j < nv && key >= f && static_cast<int>(d >> sh) == b1) atomicAdd(&h[d & msk], 1u);
   }
-  lp_reduce(S);
+  __syncwarp();
   unsigned ab2;
-  const int b2 = h256_select_asc(S, N - above, &ab2);
+  const int b2 = warp_sel_asc(h, N - above, &ab2);
+  __syncwarp();
   return kref - ((static_cast<unsigned>(b1) << sh) + static_cast<unsigned>(max(b2, 0)));
 }
 
-// keep the buffer entries with key >= f, in order; returns the new fill
-__device__ int cand_compact(RSmem& S, int fill, unsigned f, int& ph) {
-  // entries 8*tid .. 8*tid+7 (fill <= kCB = 8 * kT)
-  const int b = threadIdx.x * 8;
+// keep the warp region's entries with key >= f, in order; returns the new fill
+__device__ int wcand_compact(RSmem& S, int fill, unsigned f) {
+  const int lane = threadIdx.x & 31, base = (threadIdx.x >> 5) * kCBW;
   uint16_t k[8];
   uint32_t ix[8];
   int cnt = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const bool in = b + j < fill;
-    k[j] = in ? S.ckey[b + j] : 0;
-    ix[j] = in ? S.cidx[b + j] : 0u;
+    const int i = lane * 8 + j;
+    const bool in = i < fill;
+    k[j] = in ? S.ckey[base + i] : 0;
+    ix[j] = in ? S.cidx[base + i] : 0u;
     cnt += (in && k[j] >= f) ? 1 : 0;
   }
-  int total;
-  const int off = rscan_i(cnt, S, ph, &total);
-  __syncthreads();  // everyone has read its entries before they are overwritten
-  int o = off;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+  __syncwarp();  // every lane has read its entries before they are overwritten
+  int o = base + incl - cnt;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    if (b + j < fill && k[j] >= f) { S.ckey[o] = k[j]; S.cidx[o] = ix[j]; ++o; }
+    if (lane * 8 + j < fill && k[j] >= f) { S.ckey[o] = k[j]; S.cidx[o] = ix[j]; ++o; }
   }
+  __syncwarp();
+  return tot;
+}
+
+// Gathers the warps' regions into one buffer [0, total) in vocab order
+// (round, then warp, then position), through the stages as scratch; returns
+// total.  Every thread calls it; fill is the calling warp's region fill.
+__device__ int gather_candidates(RSmem& S, int fill, int& ph) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned* cnt = S.lp;             // [warp][round] counts
+  unsigned* obase = S.lp + 1024;    // [warp][round] output offsets
+  unsigned* rstart = S.lp + 2048;   // [warp][round] first region slot of the round
+  cnt[warp * 32 + lane] = 0u;
+  __syncwarp();
+  for (int i = lane; i < fill; i += 32) atomicAdd(&cnt[warp * 32 + (S.cidx[warp * kCBW + i] / kRound)], 1u);
+  __syncwarp();
+  const unsigned c = cnt[warp * 32 + lane];
+  unsigned incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  rstart[warp * 32 + lane] = incl - c;
+  __syncthreads();
+  // thread t <-> (round t / 32, warp t % 32): offsets in round-major order
+  int total;
+  const int off = rscan_i(static_cast<int>(cnt[(tid & 31) * 32 + (tid >> 5)]), S, ph, &total);
+  obase[(tid & 31) * 32 + (tid >> 5)] = static_cast<unsigned>(off);
+  __syncthreads();
+  uint16_t* tk = reinterpret_cast<uint16_t*>(&S.stage[0][0]);
+  uint32_t* ti = reinterpret_cast<uint32_t*>(tk + kCB);
+  for (int i = lane; i < fill; i += 32) {
+    const uint32_t ix = S.cidx[warp * kCBW + i];
+    const int rr = static_cast<int>(ix / kRound);
+    const unsigned pos = obase[warp * 32 + rr] + (static_cast<unsigned>(i) - rstart[warp * 32 + rr]);
+    tk[pos] = S.ckey[warp * kCBW + i];
+    ti[pos] = ix;
+  }
+  __syncthreads();
+  for (int i = tid; i < total; i += kT) { S.ckey[i] = tk[i]; S.cidx[i] = ti[i]; }
   __syncthreads();
   return total;
 }
 
 // ------------------------------------------------------ per-round helpers
+// packed fp32 pairs (sm_100 f32x2 ALU operations, round to nearest)
+__device__ __forceinline__ unsigned long long pk(float2 a) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk(unsigned long long r) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+  return a;
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)), "l"(pk(c)));
+  return upk(r);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+  return upk(r);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+  return upk(r);
+}
+
+// Sum over a thread's 16 entries of 2^(z log2e - c), z = y / T rounded as
+// the IEEE divide (reciprocal, residual and correction, as mass_of) or y
+// itself at T == 1; one rounding in the exponent.  GUARD drops NaN masses
+// (padding of a ragged last round).
+template <int DT, bool T1, bool GUARD>
+__device__ __forceinline__ float seg_masses(const uint32_t (&raw)[8], float T, float rT, float c) {
+  const float2 L2 = make_float2(kLog2e, kLog2e), nc2 = make_float2(-c, -c);
+  const float2 rT2 = make_float2(rT, rT), nT2 = make_float2(-T, -T);
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 y = vals2<DT>(raw[j]);
+    float2 z = y;
+    if (!T1) {
+      const float2 q = fmul2(y, rT2);
+      z = ffma2(ffma2(q, nT2, y), rT2, q);
+    }
+    const float2 a = ffma2(z, L2, nc2);
+    float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+    if (GUARD) e = make_float2(fmaxf(e.x, 0.f), fmaxf(e.y, 0.f));
+    acc = fadd2(acc, e);
+  }
+  return acc.x + acc.y;
+}
+
 // mass of an entry relative to reference q (scaled like z): mass_of with
 // the T == 1 shortcut (z = y exactly, as the divide gives)
 __device__ __forceinline__ float emass(float y, float T, float rT, float q, bool t1) {
   return t1 ? ex2_approx(__fmul_rn(__fsub_rn(y, q), kLog2e)) : mass_of(y, T, rT, q);
 }
 
-// segment s's mass rescaled to M (0 past nseg, for empty segments and for
-// references far enough below M to underflow)
+// segment s's mass rescaled to M: ss 2^(c - M log2e), with the exponent
+// rounded once (0 past nseg, for empty segments and for references far
+// enough below M to underflow; NaN sums stay NaN)
 __device__ __forceinline__ float seg_mass(const RSmem& S, int s, int nseg, float M) {
   if (s >= nseg) return 0.f;
   const float ss = S.ss[s];
-  return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmul_rn(__fsub_rn(S.sq[s], M), kLog2e))) : 0.f;
+  if (ss != ss) return ss;
+  return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmaf_rn(-M, kLog2e, S.sq[s]))) : 0.f;
 }
 
 // ------------------------------------------------------------ the kernel
@@ -541,10 +702,11 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const float ylo = __fsub_rn(C::value(k0), __fmul_rn(36.0f, T));
           kcut = (ylo > -INFINITY) ? C::from_val(ylo) : 0u;
         }
-        // Segment (round, warp) masses relative to the segment's own max z,
-        // so no mass overflows whatever M turns out to be; NaN masses
-        // (padding, NaN logits) drop out through fmaxf.
-        float rs = 0.f, qw = -INFINITY;
+        // Segment (round, warp) masses 2^(z log2e - c) against the segment's
+        // own reference c = z_max log2e, so no mass overflows whatever M
+        // turns out to be.  Full rounds skip the NaN guard: a NaN logit makes
+        // its segment sum NaN, which sends the row to the exact fallback.
+        float rs = 0.f, cq = -INFINITY;
         if (__any_sync(0xFFFFFFFFu, tm >= kcut)) {
           uint32_t tr = tm;
           if (tm > kinf) {
@@ -559,46 +721,31 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const uint32_t kw = __reduce_max_sync(0xFFFFFFFFu, tr);
           if (kw > kninf) {
             const float yw = C::value(kw);
-            qw = t1 ? yw : __fdiv_rn(yw, T);
-            if (t1) {
-              const float nq = -qw;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float2 y = vals2<DT>(raw[j]);
-                rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.x, nq), kLog2e)), 0.f);
-                rs += fmaxf(ex2_approx(__fmul_rn(__fadd_rn(y.y, nq), kLog2e)), 0.f);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float2 y = vals2<DT>(raw[j]);
-                rs += fmaxf(mass_of(y.x, T, rT, qw), 0.f);
-                rs += fmaxf(mass_of(y.y, T, rT, qw), 0.f);
-              }
-            }
+            cq = __fmul_rn(t1 ? yw : __fdiv_rn(yw, T), kLog2e);
+            if (t1) rs = (r < R - 1) ? seg_masses<DT, true, false>(raw, T, rT, cq) : seg_masses<DT, true, true>(raw, T, rT, cq);
+            else rs = (r < R - 1) ? seg_masses<DT, false, false>(raw, T, rT, cq) : seg_masses<DT, false, true>(raw, T, rT, cq);
           }
         }
         const float ws = warp_sum(rs);
-        if (lane == 0) { S.ss[r * kNW + warp] = ws; S.sq[r * kNW + warp] = qw; }
+        if (lane == 0) { S.ss[r * kNW + warp] = ws; S.sq[r * kNW + warp] = cq; }
       }
 
       if (!overflow) {
         if (r == 0) {
-          // First floor: the N0-th largest key of round 0, from counts of the
-          // 4096 keys below the round's max k0 in 256 bins of 16 (the lowest
-          // key of the bin where N0 is reached).  Top-k rows take N0 = k (the
-          // row's k-th largest key is never below it); top-p rows scale N to
-          // the round's share of the row, so about N entries pass in all.
+          // First floor: the N0-th largest of the threads' round-0 maxima,
+          // from counts of the 4096 keys below the round's max k0 in 256 bins
+          // of 16 (the lowest key of the bin where N0 is reached).  N0
+          // threads hold a key at or above it, so the round's N0-th largest
+          // key is never below it.  Top-k rows take N0 = k (the row's k-th
+          // largest key is never below it either); top-p rows scale N to the
+          // round's share of the row, so about N entries pass in all.
           const int n0 = round_len(P.V, 0);
           const int N0 = topk ? N : max(1, static_cast<int>((static_cast<long long>(N) * n0 + P.V - 1) / P.V));
-          lp_zero(S);
-#pragma unroll
-          for (int j = 0; j < kEPT; ++j) {
-            const uint32_t key = ECAH_RKEY(w, j);
-            const uint32_t d = k0 - key;
-            if (j < nv && d < 4096u) atomicAdd(&S.lp[((d >> 4) << 5) | static_cast<uint32_t>(lane)], 1u);
-          }
-          lp_reduce(S);
+          if (tid < 256) S.h256[tid] = 0u;
+          __syncthreads();
+          const uint32_t d0 = k0 - tm;
+          if (nv > 0 && d0 < 4096u) atomicAdd(&S.h256[d0 >> 4], 1u);
+          __syncthreads();
           unsigned above;
           const int b = h256_select_asc(S, static_cast<unsigned>(N0), &above);
           const uint32_t d = (b >= 0) ? static_cast<uint32_t>(b) * 16u + 15u : 4095u;
@@ -614,28 +761,43 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           for (int q = 0; q < 8; ++q) sb |= surv2(w[q], fm2) << q;
           return sb;
         };
+        // warp-level exclusive prefix of the lanes' survivor counts
+        auto lane_scan = [&](uint32_t bits, int* tot) -> int {
+          const int c = __popc(bits);
+          int incl = c;
+          if (__any_sync(0xFFFFFFFFu, c != 0)) {
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+              if (lane >= o) incl += y;
+            }
+          }
+          *tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+          return incl - c;
+        };
         uint32_t sb = survivors(f);
         int total;
-        int off = rscan_i(__popc(sb), S, ph, &total);
-        if (fill + total > kCB) {
-          // raise the floor toward the N-th largest key of the buffer and this
-          // round's survivors, drop what falls below
-          const unsigned nf = cand_nth(S, fill, w, nv, f, rmax_u(best, S, ph), static_cast<unsigned>(N));
+        int off = lane_scan(sb, &total);
+        if (fill + total > kCBW) {
+          // raise the warp's floor toward the kKeepW-th largest key of its
+          // region and this round's survivors, drop what falls below
+          const unsigned nf = wcand_nth(S, fill, w, nv, f, __reduce_max_sync(0xFFFFFFFFu, best),
+                                        static_cast<unsigned>(min(N, kKeepW)));
           if (nf > f) {
             f = nf;
-            fill = cand_compact(S, fill, f, ph);
+            fill = wcand_compact(S, fill, f);
           }
           sb = survivors(f);
-          off = rscan_i(__popc(sb), S, ph, &total);
-          if (fill + total > kCB) overflow = true;
+          off = lane_scan(sb, &total);
+          if (fill + total > kCBW) overflow = true;
         }
         if (!overflow) {
-          // append in vocab order: a survivor's slot is the thread's offset
+          // append in vocab order: a survivor's slot is the lane's offset
           // plus the survivors among its lower entries; its key is re-read
           // from the stage
           const uint16_t* sr = reinterpret_cast<const uint16_t*>(st);
           const uint32_t base = static_cast<uint32_t>(r * kRound + kEPT * tid);
-          const int o = fill + off;
+          const int o = warp * kCBW + fill + off;
           uint32_t m = sb;
           while (m) {
             const int bit = __ffs(m) - 1;
@@ -644,13 +806,21 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
             const int e = 2 * q + h;
             const uint32_t lower = (((1u << q) - 1u) * 0x00010001u) | (static_cast<uint32_t>(h) << q);
             const int pos = o + __popc(sb & lower);
-            S.ckey[pos] = static_cast<uint16_t>(key16(sr[kEPT * tid + e]));
+            S.ckey[pos] = static_cast<uint16_t>(key16(sr[kEPT * lane + e]));
             S.cidx[pos] = base + static_cast<uint32_t>(e);
           }
           fill += total;
         }
       }
     });
+
+    if (N > 0) {
+      // the warps' floors and regions -> one floor F (their max) and one
+      // buffer in vocab order holding every entry of the row with key >= F
+      overflow = __syncthreads_or(overflow) != 0;
+      if (!overflow) fill = gather_candidates(S, fill, ph);
+      f = rmax_u(f, S, ph);
+    }
 
     // ------------------------------------------------ row max and greedy
     const unsigned kmax = rmax_u(best, S, ph);
@@ -931,7 +1101,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
               if (j < nv && key >= kdraw) a += mass_of(C::value(key), T, rT, M);
             }
             a = warp_sum(a);
-            if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = M; }
+            if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = __fmul_rn(M, kLog2e); }
           });
         }
         // per-segment mass relative to M, then the segment holding u * Z
