@@ -62,6 +62,7 @@ struct RSmem {
   int wcnt[2][kNW];
   int ib[16];
   float fb[16];
+  float part[kNW];                // per-warp partial sums carried across a barrier
 };
 
 // ------------------------------------------------------------ reductions
@@ -85,6 +86,30 @@ __device__ __forceinline__ unsigned rmin_u(unsigned v, RSmem& S, int& ph) {
   unsigned m = __reduce_min_sync(0xFFFFFFFFu, S.red[ph][lane]);
   ph ^= 1;
   return m;
+}
+
+// block max of a and of b behind one barrier
+__device__ __forceinline__ void rmax2_u(unsigned a, unsigned b, RSmem& S, int& ph, unsigned* ma, unsigned* mb) {
+  a = __reduce_max_sync(0xFFFFFFFFu, a);
+  b = __reduce_max_sync(0xFFFFFFFFu, b);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { S.red[ph][warp] = a; S.wcnt[ph][warp] = static_cast<int>(b); }
+  __syncthreads();
+  *ma = __reduce_max_sync(0xFFFFFFFFu, S.red[ph][lane]);
+  *mb = __reduce_max_sync(0xFFFFFFFFu, static_cast<unsigned>(S.wcnt[ph][lane]));
+  ph ^= 1;
+}
+
+// block min of a and block max of b behind one barrier
+__device__ __forceinline__ void rminmax_u(unsigned a, unsigned b, RSmem& S, int& ph, unsigned* mn, unsigned* mx) {
+  a = __reduce_min_sync(0xFFFFFFFFu, a);
+  b = __reduce_max_sync(0xFFFFFFFFu, b);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) { S.red[ph][warp] = a; S.wcnt[ph][warp] = static_cast<int>(b); }
+  __syncthreads();
+  *mn = __reduce_min_sync(0xFFFFFFFFu, S.red[ph][lane]);
+  *mx = __reduce_max_sync(0xFFFFFFFFu, static_cast<unsigned>(S.wcnt[ph][lane]));
+  ph ^= 1;
 }
 
 // sum in warp order, then lane order (deterministic)
@@ -426,6 +451,9 @@ __device__ __forceinline__ int h256_select_asc(RSmem& S, unsigned n, unsigned* a
 // in vocab order; after the stream the regions are gathered into one buffer
 // in vocab order.
 constexpr int kCBW = kCB / kNW;           // 256
+// finishing histogram in the stages, past the gather's scratch (keys and
+// indices of kCB candidates: 48 KB)
+constexpr int kCntOff = 16384;            // words (64 KB)
 constexpr int kKeepW = kCBW / 2;          // a compaction keeps about this many
 
 // Among bins 0..255 (ascending, 8 per lane) of the warp-private histogram h,
@@ -814,19 +842,30 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       }
     });
 
+    unsigned* cnth = reinterpret_cast<unsigned*>(&S.stage[0][0]) + kCntOff;  // [kHB] counts, bin b = key kmax - b
     if (N > 0) {
       // the warps' floors and regions -> one floor F (their max) and one
       // buffer in vocab order holding every entry of the row with key >= F
       overflow = __syncthreads_or(overflow) != 0;
-      if (!overflow) fill = gather_candidates(S, fill, ph);
-      f = rmax_u(f, S, ph);
+      if (!overflow) {
+        for (int i = tid; i < kHB; i += kT) cnth[i] = 0u;   // outside the gather's scratch
+        fill = gather_candidates(S, fill, ph);
+      }
     }
+    const bool cand = N > 0 && !overflow;   // every entry with key >= f is in the buffer
 
     // ------------------------------------------------ row max and greedy
-    const unsigned kmax = rmax_u(best, S, ph);
+    unsigned kmax, fmax;
+    rmax2_u(best, N > 0 ? f : 0u, S, ph, &kmax, &fmax);
+    if (N > 0) f = fmax;
     unsigned firstc = 0xFFFFFFFFu;
-    if (best == kmax) {
+    if (cand) {
+      // the max is at or above every floor: all its entries are candidates
+      for (int i = tid; i < fill; i += kT)
+        if (S.ckey[i] == kmax) firstc = min(firstc, S.cidx[i]);
+    } else if (best == kmax) {
       // the lowest index of kmax among this thread's entries of round bround
+      // (fetching them for every thread ahead of the barrier measured slower)
       const int e0 = bround * kRound + kEPT * tid;
       float yv[kEPT];
       load16<DT>(P, row, e0, yv);
@@ -857,27 +896,32 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     } else {
       const uint32_t key_cut = zero_mass_cut<DT, 16>(M, T);
       // whole-row mass rescaled to M
+      // segment masses were taken relative to references <= M: this
+      // thread's share of the whole-row mass, summed behind the next barrier
       float S_all = 0.f;
-      bool mass_ok = true;
       if (mass_all) {
-        // segment masses were taken relative to references <= M
-        S_all = rsum_f(seg_mass(S, tid, R * kNW, M), S, ph);
-        mass_ok = isfinite(S_all);
+        const float sm = warp_sum(seg_mass(S, tid, R * kNW, M));
+        if (lane == 0) S.part[warp] = sm;
       }
-      bool fast = (!overflow || segs) && mass_ok;
       uint32_t key_lo_k = 0u, key_lo = 0u;
-      unsigned* cnth = reinterpret_cast<unsigned*>(S.stage);   // [kHB] counts, bin b = key kmax - b
       uint32_t F = f;
-      if (!overflow && (topk || topp)) {
+      const bool thr = cand && (topk || topp);
+      if (thr) {
         if (kmax >= static_cast<uint32_t>(kHB) && F < kmax - static_cast<uint32_t>(kHB - 1))
           F = kmax - static_cast<uint32_t>(kHB - 1);   // entries below stay out of the histogram
-        for (int i = tid; i < kHB; i += kT) cnth[i] = 0u;
-        __syncthreads();
         for (int i = tid; i < fill; i += kT) {
           const unsigned key = S.ckey[i];
           if (key >= F) atomicAdd(&cnth[kmax - key], 1u);
         }
-        __syncthreads();
+      }
+      __syncthreads();
+      bool mass_ok = true;
+      if (mass_all) {
+        S_all = warp_sum(S.part[lane]);
+        mass_ok = isfinite(S_all);
+      }
+      bool fast = (!overflow || segs) && mass_ok;
+      if (thr) {
         const int Bmax = static_cast<int>(kmax - F);
         // top-k: the k-th largest key among the candidates
         if (topk) {
@@ -902,9 +946,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           if (tot < k_eff || bsel == static_cast<unsigned>(INT_MAX)) {
             fast = false;
           } else {
-            if (tid == 0) S.ib[0] = static_cast<int>(tie_floor<DT, 16>(kmax - bsel, T));
-            __syncthreads();
-            key_lo_k = static_cast<uint32_t>(S.ib[0]);
+            key_lo_k = tie_floor<DT, 16>(kmax - bsel, T);   // every thread, same value
             if (key_lo_k < F) fast = false;
           }
         }
@@ -952,9 +994,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           if (!reached || bsel == static_cast<unsigned>(INT_MAX) || bsel == 0xFFFFFFFFu) {
             fast = false;
           } else {
-            if (tid == 0) S.ib[1] = static_cast<int>(max(tie_floor<DT, 16>(kmax - bsel, T), key_lo_k));
-            __syncthreads();
-            key_lo = static_cast<uint32_t>(S.ib[1]);
+            key_lo = max(tie_floor<DT, 16>(kmax - bsel, T), key_lo_k);   // every thread, same value
             if (key_lo < F) fast = false;
           }
         }
@@ -1084,8 +1124,8 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
             acc += e[j];
           }
         }
-        const unsigned pick = rmin_u(static_cast<unsigned>(mine), S, ph);
-        const unsigned lastp = rmax_u(static_cast<unsigned>(last + 1), S, ph);
+        unsigned pick, lastp;
+        rminmax_u(static_cast<unsigned>(mine), static_cast<unsigned>(last + 1), S, ph, &pick, &lastp);
         if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(S.cidx[pick]);
         else if (lastp > 0u) result = static_cast<int>(S.cidx[lastp - 1u]);
         else none = true;
@@ -1109,8 +1149,8 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         const float ex = rscan_f(v, S, ph, &Z);
         const float target = __fmul_rn(u, Z);
         const int mine = (tid < nseg && v > 0.f && ex + v > target) ? tid : INT_MAX;
-        const unsigned pick = rmin_u(static_cast<unsigned>(mine), S, ph);
-        const unsigned lastp = rmax_u(static_cast<unsigned>(v > 0.f ? tid + 1 : 0), S, ph);
+        unsigned pick, lastp;
+        rminmax_u(static_cast<unsigned>(mine), static_cast<unsigned>(v > 0.f ? tid + 1 : 0), S, ph, &pick, &lastp);
         int seg;
         bool take_last = false;
         if (pick != static_cast<unsigned>(INT_MAX)) seg = static_cast<int>(pick);
