@@ -52,6 +52,53 @@ def test_config2_mixed_full_size():
     assert nb <= 2
 
 
+def _warp_slices(V, w, rounds_of=16384, slice_len=512):
+    """Row positions one warp of the one-CTA-per-row kernel streams: entries
+    [r * 16384 + 512 w, + 512) of every 16384-entry round r."""
+    idx = np.concatenate([np.arange(r + slice_len * w, r + slice_len * (w + 1)) for r in range(0, V, rounds_of)])
+    return idx[idx < V]
+
+
+def test_row_kernel_warp_regions_and_overflow():
+    """Rows whose high logits all sit in one warp's slices, so that warp's
+    candidate region fills and is compacted, and rows whose ties at the max
+    exceed a region, so the row falls back to the radix re-stream; plus
+    top-k rows with k above a region's share.  B = 128 (row kernel)."""
+    g = torch.Generator().manual_seed(41)
+    B, V = 128, W.V_QWEN
+    x = torch.randn(B, V, generator=g) * 2.5
+    T = np.ones(B, np.float32)
+    K = np.zeros(B, np.int32)
+    P = np.ones(B, np.float32)
+    for r in range(B):
+        w = r % 32
+        sl = torch.from_numpy(_warp_slices(V, w))
+        if r < 32:              # top-p, nucleus concentrated in one warp's slices
+            x[r, sl] += 8.0
+            P[r] = (0.95, 0.6)[r % 2]
+        elif r < 64:            # top-k 200 concentrated in one warp's slices
+            x[r, sl] += 6.0
+            K[r] = 200
+            T[r] = 0.8
+        elif r < 80:            # 600 ties at the max inside one warp's slices
+            x[r, sl[:600]] = 20.0
+            K[r] = (10, 0)[r % 2]
+            P[r] = (1.0, 0.9)[r % 2]
+        elif r < 96:            # large k, spread: every warp compacts
+            K[r] = (2000, 1000)[r % 2]
+            P[r] = (1.0, 0.8)[r % 2]
+        else:                   # spread top-p / top-k + top-p
+            K[r] = (0, 50)[r % 2]
+            P[r] = (0.95, 0.9)[r % 2]
+            T[r] = (1.0, 0.7)[r % 2]
+    x = x.half()
+    U = row_uniforms(17, 2, B)
+    gpu = run_gpu(x, T, K, P, U)
+    orc = run_oracle(x, T, K, P, U)
+    nb = compare(x, T, K, P, U, gpu, orc)
+    assert nb <= 3
+
+
 @pytest.mark.parametrize("use_mval", [True, False])
 def test_config3_penalised(use_mval):
     """Zipf histories with repetition + frequency + presence penalties (32-bit
