@@ -14,6 +14,9 @@ through enough device copies to hold 3x the 126 MB L2 (11 at C2, 408 MiB) so
 every launch reads its logits from HBM.  ``e2e`` repeats the step through the public API with
 the logits in pinned host memory: H2D copy, launch, D2H of the ids.
 reference: the reference's CPU sampling path (torch port, all host threads).
+flashinfer: the reference's own GPU step (torch divides by the gathered
+mask_penalty rows and the temperature, then FlashInfer's
+top_k_top_p_sampling_from_logits), timed the same way, for comparison.
 Under torchrun each rank samples its own batch (batch-sharded, no collective);
 time is the max over ranks.
 """
@@ -378,12 +381,104 @@ def run_vocab_parallel(a):
         }), flush=True)
 
 
+def run_flashinfer(a):
+    """The reference's own GPU sampling step on the C2 inputs, for comparison
+    (ecahlang/main.py:481-491; the CUDA-graph path at :356-379 does the same
+    work): gather the batch's rows of the dense mask_penalty table
+    (manager.py:36, all ones here), divide the logits by them and by the
+    temperature, then flashinfer.sampling.top_k_top_p_sampling_from_logits(
+    ..., deterministic=True).  Timed like the native arm (CUDA-graph replays
+    over rotating inputs, CUDA events); "kernel_only" times the FlashInfer
+    call alone on pre-divided logits.  One GPU: other ranks exit at once."""
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    import flashinfer
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from ecahlang_b200 import workloads as W
+
+    w = W.config2(seed=0)
+    B, V = w.batch, w.vocab
+    bytes_in = w.logits.numel() * w.logits.element_size()
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits.to(dev) for _ in range(nbuf)]
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    mask_penalty = torch.ones(B, V, dtype=w.logits.dtype, device=dev)
+    slots = torch.arange(B, device=dev)
+    Tcol = T[:, None].to(w.logits.dtype)
+
+    def full(i):
+        y = bufs[i % nbuf] / mask_penalty.index_select(0, slots)
+        y = y / Tcol
+        return flashinfer.sampling.top_k_top_p_sampling_from_logits(y, top_k=K, top_p=P, deterministic=True)
+
+    def kernel_only(i):
+        return flashinfer.sampling.top_k_top_p_sampling_from_logits(bufs[i % nbuf], top_k=K, top_p=P,
+                                                                     deterministic=True)
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for i in range(a.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        chunk = min(a.steps, 2 * nbuf)
+        how = "CUDA-graph replays"
+        try:
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(stream)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(chunk):
+                    fn(i)
+            g.replay()
+            torch.cuda.synchronize()
+        except Exception as e:   # capture not supported: time eager launches queued back to back
+            g, how = None, f"eager launches ({type(e).__name__} under graph capture)"
+            torch.cuda.synchronize()
+        n = (a.steps // chunk) * chunk if g is not None else a.steps
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if g is not None:
+            for _ in range(n // chunk):
+                g.replay()
+        else:
+            for i in range(n):
+                fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / n, n, how
+
+    ms_full, n_full, how_full = timed(full)
+    ms_k, n_k, how_k = timed(kernel_only)
+    peak, peak_kind = _peaks()
+    alg = w.algorithmic_bytes() + B * (4 + 4 + 4 + 4)
+    print(json.dumps({
+        "impl": "flashinfer", "metric": METRIC, "value": B / (ms_full / 1e3), "unit": "rows/s", "n_gpus": 1,
+        "steps": n_full, "warmup": a.warmup, "ms_per_step": ms_full, "us_per_step": 1e3 * ms_full,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "c2_mixed B=128 V=151936 fp16 (configs[1])", "batch_per_gpu": B, "vocab": V,
+                   "l2": f"inputs rotate through {nbuf} device copies ({nbuf * bytes_in / 2**20:.0f} MiB > 126 MiB L2)",
+                   "path": "mask_penalty row gather, / mask_penalty, / temperature, "
+                           f"flashinfer {flashinfer.__version__} top_k_top_p_sampling_from_logits(deterministic=True)",
+                   "launch": how_full},
+        "roofline": {"bound": "hbm", "achieved": alg / (ms_full / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (ms_full / 1e3) / 1e9 / peak, "peak_kind": peak_kind},
+        "kernel_only": {"us_per_step": 1e3 * ms_k, "value": B / (ms_k / 1e3), "unit": "rows/s", "steps": n_k,
+                        "launch": how_k, "achieved_gbs": alg / (ms_k / 1e3) / 1e9},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--impl", choices=["native", "reference", "flashinfer"], default="native",
+                    help="reference: the CPU port of the reference path; flashinfer: the reference's "
+                         "own GPU path (torch divides + FlashInfer sampling), for comparison")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["batch", "vp"], default="batch",
                     help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split")
@@ -391,6 +486,8 @@ def main():
     a.warmup = max(3, a.warmup)
     if a.impl == "reference":
         run_reference(a)
+    elif a.impl == "flashinfer":
+        run_flashinfer(a)
     elif a.mode == "vp":
         run_vocab_parallel(a)
     else:

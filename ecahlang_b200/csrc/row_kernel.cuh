@@ -451,9 +451,11 @@ __device__ __forceinline__ int h256_select_asc(RSmem& S, unsigned n, unsigned* a
 // in vocab order; after the stream the regions are gathered into one buffer
 // in vocab order.
 constexpr int kCBW = kCB / kNW;           // 256
-// finishing histogram in the stages, past the gather's scratch (keys and
-// indices of kCB candidates: 48 KB)
+// After the stream the stages hold the gathered candidates (keys and
+// indices of up to kCB: 48 KB) and, past them, the finishing histogram.
 constexpr int kCntOff = 16384;            // words (64 KB)
+__device__ __forceinline__ uint16_t* gkey(RSmem& S) { return reinterpret_cast<uint16_t*>(&S.stage[0][0]); }
+__device__ __forceinline__ uint32_t* gidx(RSmem& S) { return reinterpret_cast<uint32_t*>(gkey(S) + kCB); }
 constexpr int kKeepW = kCBW / 2;          // a compaction keeps about this many
 
 // Among bins 0..255 (ascending, 8 per lane) of the warp-private histogram h,
@@ -572,8 +574,9 @@ __device__ int wcand_compact(RSmem& S, int fill, unsigned f) {
 }
 
 // Gathers the warps' regions into one buffer [0, total) in vocab order
-// (round, then warp, then position), through the stages as scratch; returns
-// total.  Every thread calls it; fill is the calling warp's region fill.
+// (round, then warp, then position) in the stages (gkey / gidx below);
+// returns total.  Every thread calls it; fill is the calling warp's region
+// fill.
 __device__ int gather_candidates(RSmem& S, int fill, int& ph) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned* cnt = S.lp;             // [warp][round] counts
@@ -597,8 +600,8 @@ __device__ int gather_candidates(RSmem& S, int fill, int& ph) {
   const int off = rscan_i(static_cast<int>(cnt[(tid & 31) * 32 + (tid >> 5)]), S, ph, &total);
   obase[(tid & 31) * 32 + (tid >> 5)] = static_cast<unsigned>(off);
   __syncthreads();
-  uint16_t* tk = reinterpret_cast<uint16_t*>(&S.stage[0][0]);
-  uint32_t* ti = reinterpret_cast<uint32_t*>(tk + kCB);
+  uint16_t* tk = gkey(S);
+  uint32_t* ti = gidx(S);
   for (int i = lane; i < fill; i += 32) {
     const uint32_t ix = S.cidx[warp * kCBW + i];
     const int rr = static_cast<int>(ix / kRound);
@@ -606,8 +609,6 @@ __device__ int gather_candidates(RSmem& S, int fill, int& ph) {
     tk[pos] = S.ckey[warp * kCBW + i];
     ti[pos] = ix;
   }
-  __syncthreads();
-  for (int i = tid; i < total; i += kT) { S.ckey[i] = tk[i]; S.cidx[i] = ti[i]; }
   __syncthreads();
   return total;
 }
@@ -862,7 +863,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     if (cand) {
       // the max is at or above every floor: all its entries are candidates
       for (int i = tid; i < fill; i += kT)
-        if (S.ckey[i] == kmax) firstc = min(firstc, S.cidx[i]);
+        if (gkey(S)[i] == kmax) firstc = min(firstc, gidx(S)[i]);
     } else if (best == kmax) {
       // the lowest index of kmax among this thread's entries of round bround
       // (fetching them for every thread ahead of the barrier measured slower)
@@ -910,7 +911,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         if (kmax >= static_cast<uint32_t>(kHB) && F < kmax - static_cast<uint32_t>(kHB - 1))
           F = kmax - static_cast<uint32_t>(kHB - 1);   // entries below stay out of the histogram
         for (int i = tid; i < fill; i += kT) {
-          const unsigned key = S.ckey[i];
+          const unsigned key = gkey(S)[i];
           if (key >= F) atomicAdd(&cnth[kmax - key], 1u);
         }
       }
@@ -1107,7 +1108,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const int i = b0 + j;
           e[j] = 0.f;
           if (i < fill) {
-            const uint32_t key = S.ckey[i];
+            const uint32_t key = gkey(S)[i];
             if (key >= kdraw) e[j] = mass_of(C::value(key), T, rT, M);
           }
           s8 += e[j];
@@ -1126,8 +1127,8 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         }
         unsigned pick, lastp;
         rminmax_u(static_cast<unsigned>(mine), static_cast<unsigned>(last + 1), S, ph, &pick, &lastp);
-        if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(S.cidx[pick]);
-        else if (lastp > 0u) result = static_cast<int>(S.cidx[lastp - 1u]);
+        if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(gidx(S)[pick]);
+        else if (lastp > 0u) result = static_cast<int>(gidx(S)[lastp - 1u]);
         else none = true;
       } else {
         // segment sums: from the stream (whole distribution) or a re-stream
