@@ -293,9 +293,9 @@ def run_native(a):
                          "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke},
-            # one kernel per sampler launch at B >= 96 (one CTA per row), two below
+            # one kernel per sampler launch at B >= 32 (one CTA per row), two below
             # (chunk scan + row finish); no other kernels run in the timed region
-            "gpu_launches": a.steps * (1 if B >= 96 else 2),
+            "gpu_launches": a.steps * (1 if B >= 32 else 2),
             "clocks": clk.summary(),
         }
         if ws == 1 and not a.no_cpu_baseline:

@@ -105,8 +105,10 @@ static bool stream_layout(long long B, int V, StreamLayout* L) {
 static bool stream_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
 
 // One CTA per row leaves SMs idle for small batches; below this the rows are
-// split into chunks across all SMs instead (stream_kernel.cuh).
-static constexpr int kRowKernelMinBatch = 96;
+// split into chunks across all SMs instead (stream_kernel.cuh).  On the B200
+// the row kernel is the faster of the two from 32 rows up on mixed batches
+// (C2-like rows: 31.1 vs 33.9 us at B = 32, 31.3 vs 41.2 us at B = 64).
+static constexpr int kRowKernelMinBatch = 32;
 
 // SM count of the current device, looked up once per device.
 static int device_sms() {
