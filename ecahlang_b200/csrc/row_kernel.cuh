@@ -63,6 +63,7 @@ struct RSmem {
   int ib[16];
   float fb[16];
   float part[kNW];                // per-warp partial sums carried across a barrier
+  unsigned pend[kMaxRounds];      // split rows: end of each part's candidates in the merged order
 };
 
 // ------------------------------------------------------------ reductions
@@ -313,7 +314,7 @@ __device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
   }
 }
 
-// Streams the whole row through the per-warp pipelines and calls
+// Streams rounds [r0, r1) of the row through the per-warp pipelines and calls
 // fn(r, st, raw, w, nv) once per round with the warp's stage (its slice) and
 // the thread's raw words and keys (nv of its 16 entries are in the row; the
 // rest are padding, key 0).  Warps run through the rounds independently: fn
@@ -321,19 +322,19 @@ __device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
 // round.  The next rounds are in flight while fn runs; the stage stays intact
 // until fn returns.  Ends with a block barrier.
 template <int DT, typename Fn>
-__device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
+__device__ void stream_row(const KParams& P, RSmem& S, int row, int r0, int r1, Fn&& fn) {
   const int R = (P.V + kRound - 1) / kRound;
   const bool pen = row_has_penalty(P, row);
   const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
                                                      static_cast<long long>(row) * P.row_stride);
   // rounds that need completing: all (unaligned rows, penalties), else a ragged last one
-  const int rc = (!P.vec_ok || pen) ? 0 : ((P.V % kRound) ? R - 1 : R);
+  const int rc = (!P.vec_ok || pen) ? r0 : ((P.V % kRound) ? R - 1 : R);
   __syncthreads();  // the stages may have served as finishing scratch
   for (int s = 0; s < kStages - 1; ++s) {
-    if (s < R) issue_slice(P, wstage(S, s), row4, s);
+    if (r0 + s < r1) issue_slice(P, wstage(S, (r0 + s) % kStages), row4, r0 + s);
     cp_async_commit();
   }
-  for (int r = 0; r < R; ++r) {
+  for (int r = r0; r < r1; ++r) {
     cp_async_wait_group<kStages - 2>();
     // the slice of round r landed for the warp, and the warp is done with
     // round r - 1, whose stage the next copy reuses
@@ -343,7 +344,7 @@ __device__ void stream_row(const KParams& P, RSmem& S, int row, Fn&& fn) {
     uint32_t raw[8], w[8];
     round_load(st, raw, w);
     const int nx = r + kStages - 1;
-    if (nx < R) issue_slice(P, wstage(S, nx % kStages), row4, nx);
+    if (nx < r1) issue_slice(P, wstage(S, nx % kStages), row4, nx);
     cp_async_commit();
     const int nv = (r < R - 1) ? kEPT : max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
     fn(r, static_cast<const uint4*>(st), raw, w, nv);
@@ -445,6 +446,11 @@ __device__ __forceinline__ int h256_select_asc(RSmem& S, unsigned n, unsigned* a
   *above = static_cast<unsigned>(S.ib[15]);
   return S.ib[14];
 }
+
+// what one part of a split row hands to the part that finishes the row
+struct PartHdr {
+  unsigned kmax, first, floor, fill, overflow, pad0, pad1, pad2;
+};
 
 // ------------------------------------------------------- per-warp candidates
 // Warp w keeps its candidates in region [w kCBW, (w + 1) kCBW) of the buffer,
@@ -613,6 +619,144 @@ __device__ int gather_candidates(RSmem& S, int fill, int& ph) {
   return total;
 }
 
+// Rows split over PP CTAs: each part publishes its max, first index of it,
+// floor, candidates and segment masses; the last part to arrive merges them
+// (max, first, floor, fill, overflow, cand in m; candidates into the stages;
+// segment masses into S) and returns true to finish the row.  No CTA waits
+// on another.  Kept out of line: it runs once per part.
+struct PartState {
+  unsigned kmax, first, f;
+  int fill;
+  bool overflow, cand;
+};
+
+__device__ __noinline__ bool part_exchange(const KParams& P, RSmem& S, int row, int part, int PP, int r0, int r1,
+                                           int R, int N, bool mass_all, int& ph, PartState& m) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned kmax = m.kmax, first = m.first, f = m.f;
+  int fill = m.fill;
+  bool overflow = m.overflow, cand = m.cand;
+    // ---------------------------------------- rows split over PP CTAs
+    // Each part publishes its max, first index of it, floor, candidates
+    // and segment masses; the last part to arrive merges them and finishes
+    // the row (no CTA waits on another).
+    PartHdr* hdr = static_cast<PartHdr*>(P.part_hdr) + static_cast<size_t>(row) * PP;
+    unsigned long long* pc = P.part_cand + (static_cast<size_t>(row) * PP + part) * kCB;
+    float2* pseg = P.part_seg + static_cast<size_t>(row) * (kMaxRounds * kNW);
+    if (cand)
+      for (int i = tid; i < fill; i += kT)
+        pc[i] = (static_cast<unsigned long long>(gkey(S)[i]) << 32) | gidx(S)[i];
+    if (mass_all)
+      for (int i = r0 * kNW + tid; i < r1 * kNW; i += kT) pseg[i] = make_float2(S.ss[i], S.sq[i]);
+    if (tid == 0) {
+      PartHdr h;
+      h.kmax = kmax; h.first = first; h.floor = f; h.fill = static_cast<unsigned>(cand ? fill : 0);
+      h.overflow = overflow ? 1u : 0u; h.pad0 = h.pad1 = h.pad2 = 0u;
+      hdr[part] = h;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) S.ib[6] = (atomicAdd(P.part_arrive + row, 1u) == static_cast<unsigned>(PP - 1)) ? 1 : 0;
+    __syncthreads();
+    if (S.ib[6] == 0) return false;   // another part finishes the row
+    __threadfence();
+    if (tid == 0) P.part_arrive[row] = 0u;   // ready for the next launch
+    // the parts in order (lane q of warp 0 reads part q's header): the row
+    // max, the first index of it (in the first part holding it), the
+    // highest floor, any overflow, and where each part's candidates start
+    if (warp == 0) {
+      const bool has = lane < PP;
+      PartHdr h{};
+      if (has) {
+        h.kmax = __ldcg(&hdr[lane].kmax);
+        h.first = __ldcg(&hdr[lane].first);
+        h.floor = __ldcg(&hdr[lane].floor);
+        h.fill = __ldcg(&hdr[lane].fill);
+        h.overflow = __ldcg(&hdr[lane].overflow);
+      }
+      const unsigned km = __reduce_max_sync(0xFFFFFFFFu, has ? h.kmax : 0u);
+      const unsigned at = __ballot_sync(0xFFFFFFFFu, has && h.kmax == km);
+      const unsigned fl = __shfl_sync(0xFFFFFFFFu, h.first, __ffs(at) - 1);
+      const unsigned fr = __reduce_max_sync(0xFFFFFFFFu, has ? h.floor : 0u);
+      const unsigned ov = __reduce_or_sync(0xFFFFFFFFu, has ? h.overflow : 0u);
+      unsigned incl = has ? h.fill : 0u;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      S.pend[lane] = incl;   // inclusive end of part lane's candidates
+      if (lane == 0) { S.ib[7] = static_cast<int>(km); S.ib[8] = static_cast<int>(fl); S.ib[9] = static_cast<int>(fr); S.ib[10] = static_cast<int>(ov); }
+    }
+    __syncthreads();
+    kmax = static_cast<unsigned>(S.ib[7]);
+    first = static_cast<unsigned>(S.ib[8]);
+    if (N > 0) { f = static_cast<unsigned>(S.ib[9]); overflow = S.ib[10] != 0; }
+    cand = N > 0 && !overflow;
+    if (cand) {
+      // every part's candidates with key >= f, in vocab order: thread t
+      // takes 8 consecutive entries of the parts' concatenated lists per pass
+      const int total = static_cast<int>(S.pend[PP - 1]);
+      int base = 0;
+      for (int g0 = 0; g0 < total && base <= kCB; g0 += kT * 8) {
+        // addresses first (the part boundary is walked once per thread),
+        // then all 8 loads in flight together, then the filter
+        const unsigned long long* src[8];
+        int g = g0 + tid * 8, q = 0;
+        while (q < PP - 1 && g < total && static_cast<int>(S.pend[q]) <= g) ++q;
+#pragma unroll
+        for (int j = 0; j < 8; ++j, ++g) {
+          src[j] = nullptr;
+          if (g < total) {
+            while (static_cast<int>(S.pend[q]) <= g) ++q;   // the part holding position g
+            const int start = q ? static_cast<int>(S.pend[q - 1]) : 0;
+            src[j] = P.part_cand + (static_cast<size_t>(row) * PP + q) * kCB + (g - start);
+          }
+        }
+        unsigned long long e8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e8[j] = src[j] ? __ldcg(src[j]) : 0ull;
+        int c = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (static_cast<unsigned>(e8[j] >> 32) >= f) ++c;
+          else e8[j] = 0ull;
+        }
+        int tot;
+        int o = base + rscan_i(c, S, ph, &tot);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (e8[j] != 0ull) {   // key >= f >= 1, never a zero word
+            if (o < kCB) {
+              gkey(S)[o] = static_cast<uint16_t>(e8[j] >> 32);
+              gidx(S)[o] = static_cast<uint32_t>(e8[j]);
+            }
+            ++o;
+          }
+        }
+        base += tot;
+      }
+      if (base > kCB) {
+        overflow = true;
+        cand = false;
+      } else {
+        fill = base;
+      }
+    }
+    if (mass_all)
+      for (int i = tid; i < R * kNW; i += kT) {
+        const int rr = i / kNW;
+        if (rr < r0 || rr >= r1) {
+          const float2 v = __ldcg(&pseg[i]);
+          S.ss[i] = v.x;
+          S.sq[i] = v.y;
+        }
+      }
+    __syncthreads();
+  m.kmax = kmax; m.first = first; m.f = f; m.fill = fill; m.overflow = overflow; m.cand = cand;
+  return true;
+}
+
 // ------------------------------------------------------ per-round helpers
 // packed fp32 pairs (sm_100 f32x2 ALU operations, round to nearest)
 __device__ __forceinline__ unsigned long long pk(float2 a) {
@@ -683,15 +827,18 @@ __device__ __forceinline__ float seg_mass(const RSmem& S, int s, int nseg, float
 }
 
 // ------------------------------------------------------------ the kernel
-template <int DT>
+template <int DT, bool SPLIT>
 __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
   using C = Codec<DT, 16>;
   extern __shared__ __align__(16) unsigned char dsm[];
   RSmem& S = *reinterpret_cast<RSmem*>(dsm);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = (P.V + kRound - 1) / kRound;
+  const int PP = SPLIT ? P.parts : 1;   // CTAs per row: each streams a run of rounds
 
-  for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
+  for (int unit = blockIdx.x; unit < P.B * PP; unit += gridDim.x) {
+    const int row = unit / PP, part = unit - row * PP;
+    const int r0 = (R * part) / PP, r1 = (R * (part + 1)) / PP;
     int ph = 0;
     const float T = P.temperature[row];
     const int kk = P.top_k[row];
@@ -708,7 +855,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
 
     // running state
     unsigned best = 0u;       // thread max key
-    int bround = 0;           // first round where this thread met it
+    int bround = r0;          // first round where this thread met it
     unsigned f = 0u;          // candidate floor
     int fill = 0;
     bool overflow = (N == 0);
@@ -716,16 +863,16 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     uint32_t kcut = 0u;       // mass rows: warps whose keys all lie below skip their masses
     const uint32_t kinf = C::from_val(INFINITY), kninf = C::from_val(-INFINITY);
 
-    stream_row<DT>(P, S, row, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+    stream_row<DT>(P, S, row, r0, r1, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
       const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
                                   max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
       const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);  // padding keys are 0
       if (tm > best) { best = tm; bround = r; }
-      uint32_t k0 = 0u;  // round-0 max (round 0 only)
-      if (r == 0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
+      uint32_t k0 = 0u;  // max of the part's first round (that round only)
+      if (r == r0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
 
       if (mass_all) {
-        if (r == 0) {
+        if (r == r0) {
           // entries with y below y0 - 36 T have mass below e^-36 relative to
           // the row max; all of them together stay below V e^-36 < 1e-9 of S
           const float ylo = __fsub_rn(C::value(k0), __fmul_rn(36.0f, T));
@@ -760,7 +907,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       }
 
       if (!overflow) {
-        if (r == 0) {
+        if (r == r0) {
           // First floor: the N0-th largest of the threads' round-0 maxima,
           // from counts of the 4096 keys below the round's max k0 in 256 bins
           // of 16 (the lowest key of the bin where N0 is reached).  N0
@@ -768,7 +915,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           // key is never below it.  Top-k rows take N0 = k (the row's k-th
           // largest key is never below it either); top-p rows scale N to the
           // round's share of the row, so about N entries pass in all.
-          const int n0 = round_len(P.V, 0);
+          const int n0 = round_len(P.V, r0);
           const int N0 = topk ? N : max(1, static_cast<int>((static_cast<long long>(N) * n0 + P.V - 1) / P.V));
           if (tid < 256) S.h256[tid] = 0u;
           __syncthreads();
@@ -853,7 +1000,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         fill = gather_candidates(S, fill, ph);
       }
     }
-    const bool cand = N > 0 && !overflow;   // every entry with key >= f is in the buffer
+    bool cand = N > 0 && !overflow;   // every entry with key >= f is in the buffer
 
     // ------------------------------------------------ row max and greedy
     unsigned kmax, fmax;
@@ -874,7 +1021,13 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       for (int j = 0; j < kEPT; ++j)
         if (firstc == 0xFFFFFFFFu && e0 + j < P.V && C::from_val(yv[j]) == kmax) firstc = static_cast<unsigned>(e0 + j);
     }
-    const unsigned first = rmin_u(firstc, S, ph);
+    unsigned first = rmin_u(firstc, S, ph);
+
+    if constexpr (SPLIT) {
+      PartState m{kmax, first, f, fill, overflow, cand};
+      if (!part_exchange(P, S, row, part, PP, r0, r1, R, N, mass_all, ph, m)) continue;   // another part finishes
+      kmax = m.kmax; first = m.first; f = m.f; fill = m.fill; overflow = m.overflow; cand = m.cand;
+    }
     const float ymax = C::value(kmax);
     const float M = __fdiv_rn(ymax, T);
     const bool greedy = !(T > 0.f) || !isfinite(M);
@@ -1006,7 +1159,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         key_lo_k = 0u;
         if (topk) {
           lp_zero(S);
-          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j)
               if (j < nv) atomicAdd(&S.lp[((ECAH_RKEY(w, j) >> 8) << 5) | static_cast<uint32_t>(lane)], 1u);
@@ -1015,7 +1168,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           unsigned above;
           const int hb = h256_select_desc(S, static_cast<unsigned>(k_eff), &above);
           lp_zero(S);
-          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -1034,7 +1187,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const uint32_t klo = max(key_lo_k, key_cut);
           lp_zero(S);
           float sk = 0.f;
-          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -1065,7 +1218,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           const int hb = S.ib[2];
           lp_zero(S);
           float above = 0.f;
-          stream_row<DT>(P, S, row, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const uint32_t key = ECAH_RKEY(w, j);
@@ -1134,7 +1287,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         // segment sums: from the stream (whole distribution) or a re-stream
         const int nseg = R * kNW;
         if (!(fast && segs)) {
-          stream_row<DT>(P, S, row, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+          stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
             float a = 0.f;
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {

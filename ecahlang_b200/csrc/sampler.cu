@@ -3,6 +3,7 @@
 // keys: fp16/bf16 logits without additive penalties, given the full workspace)
 // and sampler_kernel.cuh (everything else).
 
+#include <algorithm>
 #include <cstdio>
 
 #include "row_kernel.cuh"
@@ -79,37 +80,6 @@ static constexpr size_t kMaxDynSmem = 128 * 1024;
 // the cluster kernel's workspace: the Philox completion counter
 static constexpr size_t kMinWorkspace = 256;
 
-// Workspace of the streaming kernels: [0, 256) the Philox completion counter,
-// then chunk summaries, finished-row data and the candidate lists, each
-// region 256-byte aligned.
-struct StreamLayout {
-  int NC;
-  size_t sums, fin, cand, total;
-};
-
-static bool stream_layout(long long B, int V, StreamLayout* L) {
-  if (B < 0 || V < 1) return false;
-  const int NC = (V + kSCH - 1) / kSCH;
-  if (NC > kSMaxChunks) return false;
-  auto a256 = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  const size_t b = static_cast<size_t>(B);
-  size_t off = kMinWorkspace;
-  L->sums = off; off += a256(b * NC * sizeof(ChunkSum));
-  L->fin = off; off += a256(b * sizeof(RowFin));
-  L->cand = off; off += a256(b * NC * kSCap * sizeof(unsigned));
-  L->NC = NC;
-  L->total = off;
-  return true;
-}
-
-static bool stream_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
-
-// One CTA per row leaves SMs idle for small batches; below this the rows are
-// split into chunks across all SMs instead (stream_kernel.cuh).  On the B200
-// the row kernel is the faster of the two from 32 rows up on mixed batches
-// (C2-like rows: 31.1 vs 33.9 us at B = 32, 31.3 vs 41.2 us at B = 64).
-static constexpr int kRowKernelMinBatch = 32;
-
 // SM count of the current device, looked up once per device.
 static int device_sms() {
   constexpr int kMaxDev = 64;
@@ -122,6 +92,73 @@ static int device_sms() {
   cache[dev] = sms;
   return sms;
 }
+
+// Workspace header: [0, 256) the Philox completion counter and the error
+// word; [256, 4096) one arrival counter per row split over several CTAs.
+// Both are left at zero by every launch, at fixed offsets for any batch.
+static constexpr size_t kHeaderBytes = 4096;
+static constexpr int kMinParts = 4;
+static constexpr int kMaxSplitRows = static_cast<int>((kHeaderBytes - kMinWorkspace) / sizeof(unsigned));
+
+// CTAs per row of the row kernel: enough to occupy the SMs of the current
+// device when the batch is small, at most one per 16384-entry round.
+static int row_parts(long long B, int V) {
+  const int R = (V + rk::kRound - 1) / rk::kRound;
+  const int sms = device_sms();
+  if (B <= 0 || B > kMaxSplitRows || sms <= 0 || V > rk::kMaxRounds * rk::kRound) return 1;
+  // two or three parts per row cost more in the exchange than they save
+  const long long p = sms / B;
+  return static_cast<int>(p < kMinParts ? 1 : (p > R ? R : p));
+}
+
+static size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// bytes of the per-part regions of a row kernel launch at batch B (0 when
+// its rows are not split)
+static size_t parts_bytes(long long B, int V) {
+  const size_t pp = static_cast<size_t>(row_parts(B, V));
+  if (pp < 2) return 0;
+  const size_t b = static_cast<size_t>(B);
+  return a256(b * pp * sizeof(rk::PartHdr)) + a256(b * pp * rk::kCB * sizeof(unsigned long long)) +
+         a256(b * rk::kMaxRounds * rk::kNW * sizeof(float2));
+}
+
+// Workspace regions after the header, each 256-byte aligned: the streaming
+// kernels' chunk summaries, finished-row data (also the row kernel's) and
+// candidate lists; then, for rows split over several CTAs of the row kernel,
+// the parts' headers, candidates and segment masses.  Every region is
+// written before it is read within a launch.
+struct StreamLayout {
+  int NC, parts;
+  size_t sums, fin, cand, total_stream;
+  size_t hdr, pcand, pseg, total;
+};
+
+static bool stream_layout(long long B, int V, StreamLayout* L) {
+  if (B < 0 || V < 1) return false;
+  const int NC = (V + kSCH - 1) / kSCH;
+  if (NC > kSMaxChunks) return false;
+  const size_t b = static_cast<size_t>(B);
+  size_t off = kHeaderBytes;
+  L->sums = off; off += a256(b * NC * sizeof(ChunkSum));
+  L->fin = off; off += a256(b * sizeof(RowFin));
+  L->cand = off; off += a256(b * NC * kSCap * sizeof(unsigned));
+  L->NC = NC;
+  L->total_stream = off;
+  L->parts = row_parts(B, V);
+  const size_t pp = static_cast<size_t>(L->parts);
+  L->hdr = L->pcand = L->pseg = 0;
+  if (pp > 1) {
+    L->hdr = off; off += a256(b * pp * sizeof(rk::PartHdr));
+    L->pcand = off; off += a256(b * pp * rk::kCB * sizeof(unsigned long long));
+    L->pseg = off; off += a256(b * rk::kMaxRounds * rk::kNW * sizeof(float2));
+  }
+  L->total = off;
+  return true;
+}
+
+static bool stream_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
+
 
 // CTAs of the persistent streaming kernel that fit on the current device at
 // once (occupancy x SM count), looked up once per device and kernel.
@@ -186,8 +223,13 @@ const char* ecah_status_string(int s) {
 
 size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype) {
   StreamLayout L;
-  if (stream_dtype(dtype) && stream_layout(batch, vocab, &L)) return L.total;
-  return kMinWorkspace;
+  if (!stream_dtype(dtype) || !stream_layout(batch, vocab, &L)) return kMinWorkspace;
+  // any launch of at most `batch` rows fits: the stream regions grow with the
+  // batch, the split-row regions peak at some smaller batch
+  size_t split = 0;
+  const int top = batch < kMaxSplitRows ? batch : kMaxSplitRows;
+  for (int b = 1; b <= top; ++b) split = std::max(split, parts_bytes(b, vocab));
+  return L.total_stream + split;
 }
 
 // Not exported: the least workspace any launch accepts (the cluster kernel's).
@@ -233,40 +275,46 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   P.vec_ok = (reinterpret_cast<uintptr_t>(a->logits) % 16 == 0) && ((a->row_stride * es) % 16 == 0);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  // row kernel: 16-bit keys, one CTA per row, for batches that occupy most SMs
+  // row kernel: 16-bit keys; one CTA per row, or a row split over several
+  // CTAs when the batch leaves SMs idle
   StreamLayout L;
   const bool k16 = stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES);
-  if (k16 && a->batch >= kRowKernelMinBatch && a->vocab <= rk::kMaxRounds * rk::kRound &&
-      stream_layout(a->batch, a->vocab, &L) && a->workspace_bytes >= L.total) {
+  if (k16 && a->vocab <= rk::kMaxRounds * rk::kRound && stream_layout(a->batch, a->vocab, &L) &&
+      a->workspace_bytes >= L.total) {
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P.NC = L.NC;
     P.ws_sums = ws + L.sums;
     P.ws_fin = ws + L.fin;
     P.ws_cand = reinterpret_cast<unsigned*>(ws + L.cand);
+    P.parts = L.parts;
+    P.part_arrive = L.parts > 1 ? reinterpret_cast<unsigned*>(ws + kMinWorkspace) : nullptr;
+    P.part_hdr = L.parts > 1 ? ws + L.hdr : nullptr;
+    P.part_cand = L.parts > 1 ? reinterpret_cast<unsigned long long*>(ws + L.pcand) : nullptr;
+    P.part_seg = L.parts > 1 ? reinterpret_cast<float2*>(ws + L.pseg) : nullptr;
     const int smem = static_cast<int>(sizeof(rk::RSmem));
     const int sms = device_sms();
     if (sms <= 0) return ECAH_ERR_LAUNCH;
-    const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
+    const long long units = static_cast<long long>(a->batch) * L.parts;
+    const dim3 grid(static_cast<unsigned>(units < sms ? units : sms));
     const dim3 all(static_cast<unsigned>(static_cast<long long>(a->batch) * L.NC));
-    if (a->dtype == ECAH_DTYPE_F16) {
-      if (cudaFuncSetAttribute(rk::row_sample_kernel<ECAH_DTYPE_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem) != cudaSuccess)
-        return ECAH_ERR_LAUNCH;
-      rk::row_sample_kernel<ECAH_DTYPE_F16><<<grid, rk::kT, smem, s>>>(P);
-      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
-    } else {
-      if (cudaFuncSetAttribute(rk::row_sample_kernel<ECAH_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem) != cudaSuccess)
-        return ECAH_ERR_LAUNCH;
-      rk::row_sample_kernel<ECAH_DTYPE_BF16><<<grid, rk::kT, smem, s>>>(P);
-      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
+    KernelFn fn = nullptr;
+    if (a->dtype == ECAH_DTYPE_F16)
+      fn = L.parts > 1 ? rk::row_sample_kernel<ECAH_DTYPE_F16, true> : rk::row_sample_kernel<ECAH_DTYPE_F16, false>;
+    else
+      fn = L.parts > 1 ? rk::row_sample_kernel<ECAH_DTYPE_BF16, true> : rk::row_sample_kernel<ECAH_DTYPE_BF16, false>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return ECAH_ERR_LAUNCH;
+    fn<<<grid, rk::kT, smem, s>>>(P);
+    if (a->probs_out) {
+      if (a->dtype == ECAH_DTYPE_F16) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
+      else stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
     }
     return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
   }
 
-  // streaming kernel: 16-bit keys and the full workspace
+  // streaming kernel: 16-bit keys and its share of the workspace
   if (stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES) && stream_layout(a->batch, a->vocab, &L) &&
-      a->workspace_bytes >= L.total && static_cast<long long>(a->batch) * L.NC <= 0x7FFFFFFFLL) {
+      a->workspace_bytes >= L.total_stream && static_cast<long long>(a->batch) * L.NC <= 0x7FFFFFFFLL) {
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P.NC = L.NC;
     P.ws_sums = ws + L.sums;

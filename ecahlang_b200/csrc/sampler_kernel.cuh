@@ -79,6 +79,12 @@ struct KParams {
   int vec_ok;              // 16-byte aligned rows
   float fx_scale;          // fixed-point scale of level-0 masses (2^s)
   float fx_inv;            // 2^-s
+  // row kernel (row_kernel.cuh) with a row split over several CTAs
+  int parts;                        // CTAs per row, >= 1
+  unsigned* part_arrive;            // [B] parts of the row done so far (left 0)
+  void* part_hdr;                   // [B, parts] per-part results
+  unsigned long long* part_cand;    // [B, parts, kCB] candidates: key << 32 | row index
+  float2* part_seg;                 // [B, 32 rounds x 32 warps] segment (mass, reference)
 };
 
 constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private

@@ -114,9 +114,17 @@ def workspace_bytes(batch: int, vocab: int, dtype: torch.dtype) -> int:
 
 
 def new_workspace(batch: int, vocab: int, dtype: torch.dtype, device="cuda") -> torch.Tensor:
-    """Zero-filled workspace; every launch leaves it zero-filled again.  One
-    workspace per stream that may run a sampler launch concurrently."""
-    return torch.zeros(workspace_bytes(batch, vocab, dtype), dtype=torch.uint8, device=device)
+    """Zero-filled workspace for launches of up to `batch` rows on `device`
+    (its size depends on the device's SM count); every launch leaves its
+    counters at zero again.  One workspace per stream that may run a sampler
+    launch concurrently."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and torch.cuda.is_available():
+        with torch.cuda.device(dev):
+            n = workspace_bytes(batch, vocab, dtype)
+    else:
+        n = workspace_bytes(batch, vocab, dtype)
+    return torch.zeros(n, dtype=torch.uint8, device=dev)
 
 
 def new_philox_state(seed: int, offset: int = 0, device="cuda") -> torch.Tensor:

@@ -110,15 +110,19 @@ typedef struct ecah_sampler_args {
                                  kept sets are {i : y'_i >= threshold}            */
   float* probs_out;           /* [B, vocab] renormalised probabilities of the final
                                  set (0 elsewhere); greedy rows get a one-hot row */
-  void* workspace;            /* >= ecah_sampler_workspace_bytes(), zero-filled once
-                                 before first use; left zero-filled by every launch */
+  void* workspace;            /* >= ecah_sampler_workspace_bytes(B, vocab, dtype) for
+                                 some B >= batch, zero-filled once before first use.
+                                 Its first 4096 bytes hold counters that every launch
+                                 leaves at zero; the rest is scratch.               */
   size_t workspace_bytes;
 } ecah_sampler_args;
 
 ECAH_API int ecah_sampler_abi_version(void);
 ECAH_API const char* ecah_status_string(int status);
 
-/* Workspace needed by ecah_sampler_launch for this shape.  New entry point:
+/* Workspace for launches of up to `batch` rows of this vocabulary and dtype
+ * on the current device (small batches split rows over several CTAs, which
+ * needs room that depends on the device's SM count).  New entry point:
  * FlashInfer's sampling ops allocate their row-state buffers themselves
  * (called from ecahlang/main.py:377-379); here the caller owns them. */
 ECAH_API size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype);
