@@ -123,28 +123,23 @@ static size_t parts_bytes(long long B, int V) {
          a256(b * rk::kMaxRounds * rk::kNW * sizeof(float2));
 }
 
-// Workspace regions after the header, each 256-byte aligned: the streaming
-// kernels' chunk summaries, finished-row data (also the row kernel's) and
-// candidate lists; then, for rows split over several CTAs of the row kernel,
-// the parts' headers, candidates and segment masses.  Every region is
-// written before it is read within a launch.
-struct StreamLayout {
-  int NC, parts;
-  size_t sums, fin, cand, total_stream;
+// Row-kernel workspace regions after the header, each 256-byte aligned: the
+// finished-row data of the probability kernel, then, for rows split over
+// several CTAs, the parts' headers, candidates and segment masses.  Every
+// region is written before it is read within a launch.
+struct RowLayout {
+  int NC, parts;                    // 8192-entry chunks per row (probability kernel)
+  size_t fin, base_total;           // base_total: without the split-row regions
   size_t hdr, pcand, pseg, total;
 };
 
-static bool stream_layout(long long B, int V, StreamLayout* L) {
-  if (B < 0 || V < 1) return false;
-  const int NC = (V + kSCH - 1) / kSCH;
-  if (NC > kSMaxChunks) return false;
+static bool row_layout(long long B, int V, RowLayout* L) {
+  if (B < 0 || V < 1 || V > rk::kMaxRounds * rk::kRound) return false;
   const size_t b = static_cast<size_t>(B);
   size_t off = kHeaderBytes;
-  L->sums = off; off += a256(b * NC * sizeof(ChunkSum));
   L->fin = off; off += a256(b * sizeof(RowFin));
-  L->cand = off; off += a256(b * NC * kSCap * sizeof(unsigned));
-  L->NC = NC;
-  L->total_stream = off;
+  L->NC = (V + kSCH - 1) / kSCH;
+  L->base_total = off;
   L->parts = row_parts(B, V);
   const size_t pp = static_cast<size_t>(L->parts);
   L->hdr = L->pcand = L->pseg = 0;
@@ -157,26 +152,7 @@ static bool stream_layout(long long B, int V, StreamLayout* L) {
   return true;
 }
 
-static bool stream_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
-
-
-// CTAs of the persistent streaming kernel that fit on the current device at
-// once (occupancy x SM count), looked up once per device and kernel.
-static int stream_resident_ctas(KernelFn fn) {
-  constexpr int kMaxDev = 64;
-  static int cache[2][kMaxDev] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 0;
-  const int which = (fn == stream_scan_kernel<ECAH_DTYPE_F16>) ? 0 : 1;
-  int v = cache[which][dev];
-  if (v > 0) return v;
-  int per_sm = 0, sms = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, 0) != cudaSuccess) return 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-  v = per_sm * sms;
-  cache[which][dev] = v;
-  return v;
-}
+static bool k16_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
 
 static bool make_plan(int dtype, int V, unsigned flags, Plan* p) {
   const int kb = (dtype == ECAH_DTYPE_F32 || (flags & ECAH_FLAG_FREQ_PRES)) ? 32 : 16;
@@ -222,14 +198,14 @@ const char* ecah_status_string(int s) {
 }
 
 size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype) {
-  StreamLayout L;
-  if (!stream_dtype(dtype) || !stream_layout(batch, vocab, &L)) return kMinWorkspace;
-  // any launch of at most `batch` rows fits: the stream regions grow with the
-  // batch, the split-row regions peak at some smaller batch
+  RowLayout L;
+  if (!k16_dtype(dtype) || !row_layout(batch, vocab, &L)) return kMinWorkspace;
+  // any launch of at most `batch` rows fits: the finished-row region grows
+  // with the batch, the split-row regions peak at some smaller batch
   size_t split = 0;
   const int top = batch < kMaxSplitRows ? batch : kMaxSplitRows;
   for (int b = 1; b <= top; ++b) split = std::max(split, parts_bytes(b, vocab));
-  return L.total_stream + split;
+  return L.base_total + split;
 }
 
 // Not exported: the least workspace any launch accepts (the cluster kernel's).
@@ -277,15 +253,12 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
 
   // row kernel: 16-bit keys; one CTA per row, or a row split over several
   // CTAs when the batch leaves SMs idle
-  StreamLayout L;
-  const bool k16 = stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES);
-  if (k16 && a->vocab <= rk::kMaxRounds * rk::kRound && stream_layout(a->batch, a->vocab, &L) &&
-      a->workspace_bytes >= L.total) {
+  RowLayout L;
+  const bool k16 = k16_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES);
+  if (k16 && row_layout(a->batch, a->vocab, &L) && a->workspace_bytes >= L.total) {
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P.NC = L.NC;
-    P.ws_sums = ws + L.sums;
     P.ws_fin = ws + L.fin;
-    P.ws_cand = reinterpret_cast<unsigned*>(ws + L.cand);
     P.parts = L.parts;
     P.part_arrive = L.parts > 1 ? reinterpret_cast<unsigned*>(ws + kMinWorkspace) : nullptr;
     P.part_hdr = L.parts > 1 ? ws + L.hdr : nullptr;
@@ -308,35 +281,6 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
     if (a->probs_out) {
       if (a->dtype == ECAH_DTYPE_F16) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
       else stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
-    }
-    return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
-  }
-
-  // streaming kernel: 16-bit keys and its share of the workspace
-  if (stream_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES) && stream_layout(a->batch, a->vocab, &L) &&
-      a->workspace_bytes >= L.total_stream && static_cast<long long>(a->batch) * L.NC <= 0x7FFFFFFFLL) {
-    unsigned char* ws = static_cast<unsigned char*>(a->workspace);
-    P.NC = L.NC;
-    P.ws_sums = ws + L.sums;
-    P.ws_fin = ws + L.fin;
-    P.ws_cand = reinterpret_cast<unsigned*>(ws + L.cand);
-    const long long units = static_cast<long long>(a->batch) * L.NC;
-    const dim3 all(static_cast<unsigned>(units));
-    const dim3 rows(static_cast<unsigned>(a->batch));
-    if (a->dtype == ECAH_DTYPE_F16) {
-      const int resident = stream_resident_ctas(stream_scan_kernel<ECAH_DTYPE_F16>);
-      if (resident <= 0) return ECAH_ERR_LAUNCH;
-      const dim3 grid(static_cast<unsigned>(units < resident ? units : resident));
-      stream_scan_kernel<ECAH_DTYPE_F16><<<grid, kThreads, 0, s>>>(P);
-      stream_finish_kernel<ECAH_DTYPE_F16><<<rows, kThreads, 0, s>>>(P);
-      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
-    } else {
-      const int resident = stream_resident_ctas(stream_scan_kernel<ECAH_DTYPE_BF16>);
-      if (resident <= 0) return ECAH_ERR_LAUNCH;
-      const dim3 grid(static_cast<unsigned>(units < resident ? units : resident));
-      stream_scan_kernel<ECAH_DTYPE_BF16><<<grid, kThreads, 0, s>>>(P);
-      stream_finish_kernel<ECAH_DTYPE_BF16><<<rows, kThreads, 0, s>>>(P);
-      if (a->probs_out) stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
     }
     return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
   }
@@ -376,7 +320,7 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
 static int vp_params(const ecah_vp_args* a, vp::VParams* P) {
   if (!a) return ECAH_ERR_NULL;
   if (a->abi_version != ECAH_SAMPLER_ABI_VERSION) return ECAH_ERR_ABI;
-  if (!stream_dtype(a->dtype)) return ECAH_ERR_DTYPE;
+  if (!k16_dtype(a->dtype)) return ECAH_ERR_DTYPE;
   if (a->batch < 0 || a->vocab < 1 || a->vocab_local < 1 || a->vocab_local > vp::kMaxLocal || a->vocab_offset < 0 ||
       static_cast<long long>(a->vocab_offset) + a->vocab_local > a->vocab || a->row_stride < a->vocab_local ||
       a->cand_cap < 1 || a->world < 1 || a->world > 64 || static_cast<long long>(a->world) * a->cand_cap > vp::kMaxMerged)

@@ -69,11 +69,10 @@ struct KParams {
   float* row_stats;
   float* probs_out;
   unsigned* done_counter;  // workspace word for the Philox offset bump
-  // streaming kernel (stream_kernel.cuh): chunks per row and workspace regions
+  // row kernel and probability kernel: 8192-entry chunks per row, and the
+  // finished-row data the probability kernel reads
   int NC;
-  void* ws_sums;           // [B, NC] chunk summaries
-  unsigned* ws_cand;       // [B, NC, kSCap] candidate lists
-  void* ws_fin;            // [B] finished-row data for the probability kernel
+  void* ws_fin;            // [B] RowFin
   int CL;                  // CTAs per row (cluster size)
   int CH;                  // vocab entries per CTA (multiple of 8)
   int vec_ok;              // 16-byte aligned rows
