@@ -1,7 +1,9 @@
-// Row-per-CTA token sampler for sm_100a: one 1024-thread CTA owns a whole
-// row, streams it from HBM through a four-stage cp.async pipeline (32 KB
-// rounds), keeps every running quantity on chip and finishes the row without
-// talking to any other CTA.
+// Row-per-CTA token sampler for sm_100a: one 1024-thread CTA owns a row (or,
+// for batches that leave SMs idle, a run of the row's rounds, see
+// part_exchange), streams it from HBM through one four-stage cp.async
+// pipeline per warp (32 KB rounds, a 1 KB slice per warp), keeps every
+// running quantity on chip and finishes the row without waiting on any other
+// CTA.
 //
 // During the stream, per row mode (16-bit keys: fp16/bf16 logits):
 //   - every row: per-thread running (max key, first round holding it);
