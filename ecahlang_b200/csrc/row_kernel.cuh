@@ -185,24 +185,10 @@ __device__ __forceinline__ int round_len(int V, int r) { return min(kRound, V - 
 constexpr int kWS = kRound / kNW;         // entries of a warp slice (512)
 constexpr int kWV = kWS / 8;              // 16-byte chunks of a slice (64)
 
-// this warp's stage s
-__device__ __forceinline__ uint4* wstage(RSmem& S, int s) {
-  return &S.stage[0][0] + ((threadIdx.x >> 5) * kStages + s) * kWV;
-}
 
 // first row entry of this warp's slice of round r, and how many lie in the row
 __device__ __forceinline__ int slice_e0(int r) { return r * kRound + (threadIdx.x >> 5) * kWS; }
 __device__ __forceinline__ int slice_len(int V, int r) { return max(0, min(kWS, V - slice_e0(r))); }
-
-// cp.async of the slice's whole 16-byte chunks: lane l copies chunks l and l + 32
-__device__ __forceinline__ void issue_slice(const KParams& P, uint4* st, const uint4* row4, int r) {
-  if (!P.vec_ok) return;
-  const int nfull = slice_len(P.V, r) >> 3;
-  const uint4* s4 = row4 + (slice_e0(r) >> 3);
-  const int lane = threadIdx.x & 31;
-  if (lane < nfull) cp_async16(st + lane, s4 + lane);
-  if (lane + 32 < nfull) cp_async16(st + lane + 32, s4 + lane + 32);
-}
 
 // Whether the row has a repetition-penalty history to patch in.
 __device__ __forceinline__ bool row_has_penalty(const KParams& P, int row) {
@@ -326,14 +312,34 @@ __device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
 template <int DT, typename Fn>
 __device__ void stream_row(const KParams& P, RSmem& S, int row, int r0, int r1, Fn&& fn) {
   const int R = (P.V + kRound - 1) / kRound;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool pen = row_has_penalty(P, row);
-  const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
-                                                     static_cast<long long>(row) * P.row_stride);
+  const bool vec = P.vec_ok != 0;
   // rounds that need completing: all (unaligned rows, penalties), else a ragged last one
-  const int rc = (!P.vec_ok || pen) ? r0 : ((P.V % kRound) ? R - 1 : R);
+  const int rc = (!vec || pen) ? r0 : ((P.V % kRound) ? R - 1 : R);
+  // this thread's chunks: the warp's slice of round r starts at chunk
+  // r * kRVecs + warp * kWV; lane l copies chunks l and l + 32 of it
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
+                                                    static_cast<long long>(row) * P.row_stride) +
+                     warp * kWV + lane;
+  uint4* wst = &S.stage[0][0] + warp * (kStages * kWV);   // this warp's stages
+  const int last_nv = max(0, min(kEPT, round_len(P.V, R - 1) - kEPT * static_cast<int>(threadIdx.x)));
+  auto issue = [&](int x) {
+    if (!vec) return;
+    uint4* d = wst + (x % kStages) * kWV + lane;
+    const uint4* g = src + static_cast<long long>(x) * kRVecs;
+    if (x < R - 1) {   // whole slices
+      cp_async16(d, g);
+      cp_async16(d + 32, g + 32);
+    } else {
+      const int nfull = slice_len(P.V, x) >> 3;
+      if (lane < nfull) cp_async16(d, g);
+      if (lane + 32 < nfull) cp_async16(d + 32, g + 32);
+    }
+  };
   __syncthreads();  // the stages may have served as finishing scratch
   for (int s = 0; s < kStages - 1; ++s) {
-    if (r0 + s < r1) issue_slice(P, wstage(S, (r0 + s) % kStages), row4, r0 + s);
+    if (r0 + s < r1) issue(r0 + s);
     cp_async_commit();
   }
   for (int r = r0; r < r1; ++r) {
@@ -341,15 +347,13 @@ __device__ void stream_row(const KParams& P, RSmem& S, int row, int r0, int r1, 
     // the slice of round r landed for the warp, and the warp is done with
     // round r - 1, whose stage the next copy reuses
     __syncwarp();
-    uint4* st = wstage(S, r % kStages);
+    uint4* st = wst + (r % kStages) * kWV;
     if (r >= rc) complete_slice<DT>(P, st, row, r, pen);
     uint32_t raw[8], w[8];
     round_load(st, raw, w);
-    const int nx = r + kStages - 1;
-    if (nx < r1) issue_slice(P, wstage(S, nx % kStages), row4, nx);
+    if (r + kStages - 1 < r1) issue(r + kStages - 1);
     cp_async_commit();
-    const int nv = (r < R - 1) ? kEPT : max(0, min(kEPT, round_len(P.V, r) - kEPT * static_cast<int>(threadIdx.x)));
-    fn(r, static_cast<const uint4*>(st), raw, w, nv);
+    fn(r, static_cast<const uint4*>(st), raw, w, (r < R - 1) ? kEPT : last_nv);
   }
   cp_async_wait_group<0>();
   __syncthreads();
