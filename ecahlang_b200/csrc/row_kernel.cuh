@@ -47,6 +47,7 @@ constexpr int kDenseN = 4096;             // candidate target of top-p-only rows
 constexpr int kHB = 4096;                 // finishing histogram: keys below the row max
 constexpr int kMaxRounds = 32;            // vocab <= 32 * 16384
 constexpr int kSegs = kMaxRounds * kNW;   // (round, warp) segments of 512 entries
+constexpr int kPenCap = 896;              // history entries bucketed in shared memory per row
 // fallback level-0 fixed point: a mass <= 1 times 2^22 stays below the 2^23
 // to_fixed needs, and a lane's slot sums at most 16 * 32 masses (< 2^32)
 constexpr float kFx = 4194304.0f;
@@ -66,6 +67,11 @@ struct RSmem {
   float fb[16];
   float part[kNW];                // per-warp partial sums carried across a barrier
   unsigned pend[kMaxRounds];      // split rows: end of each part's candidates in the merged order
+  // the row's repetition-penalty history bucketed by slice (round, warp):
+  // slice s holds entries [poff[s], poff[s + 1]) of pent
+  uint16_t poff[kMaxRounds * kNW + 1];
+  uint2 pent[kPenCap];            // {offset in the slice, divisor m as float bits}
+  int pen_ok;                     // the buckets hold the whole history
 };
 
 // ------------------------------------------------------------ reductions
@@ -200,7 +206,7 @@ __device__ __forceinline__ bool row_has_penalty(const KParams& P, int row) {
 // Ragged tail / unaligned rows with plain loads, padding (key 0), penalty
 // patch, for this warp's slice.  Returns with the slice complete for the warp.
 template <int DT>
-__device__ void complete_slice(const KParams& P, uint4* st, int row, int r, bool pen) {
+__device__ void complete_slice(const KParams& P, const RSmem& S, uint4* st, int row, int r, bool pen) {
   using Dt = DType<DT>;
   const int lane = threadIdx.x & 31;
   const int n = slice_len(P.V, r);
@@ -213,20 +219,70 @@ __device__ void complete_slice(const KParams& P, uint4* st, int row, int r, bool
     __syncwarp();
   }
   if (pen) {
-    const int slot = P.row_slot[row];
-    const int len = min(P.slot_len[slot], P.hist_cap);
-    const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
-    const long long base = static_cast<long long>(slot) * P.hist_cap;
-    for (int h = lane; h < len; h += 32) {
-      const int li = P.hist_tok[base + h] - e0;
-      const int cnt = P.hist_cnt[base + h];
-      if (cnt <= 0 || li < 0 || li >= n) continue;
-      const float x = Dt::to_f32(raw[li]);
-      const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
-      raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
+    if (S.pen_ok) {
+      // this slice's bucket of the history (shared memory)
+      const int sl = r * kNW + (threadIdx.x >> 5);
+      for (int i = S.poff[sl] + lane; i < S.poff[sl + 1]; i += 32) {
+        const uint2 e = S.pent[i];
+        raw[e.x] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(Dt::to_f32(raw[e.x]), __uint_as_float(e.y)))));
+      }
+    } else {
+      const int slot = P.row_slot[row];
+      const int len = min(P.slot_len[slot], P.hist_cap);
+      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+      const long long base = static_cast<long long>(slot) * P.hist_cap;
+      for (int h = lane; h < len; h += 32) {
+        const int li = P.hist_tok[base + h] - e0;
+        const int cnt = P.hist_cnt[base + h];
+        if (cnt <= 0 || li < 0 || li >= n) continue;
+        const float x = Dt::to_f32(raw[li]);
+        const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
+        raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
+      }
     }
     __syncwarp();
   }
+}
+
+// Buckets the row's penalty history by slice in shared memory (counting sort
+// by token / 512), so each warp patches only its slice's entries every round.
+// Every thread calls it; S.pen_ok = 0 when the history does not fit (the
+// patch then scans the history in global memory).
+template <int DT>
+__device__ void bucket_penalties(const KParams& P, RSmem& S, int row, int& ph) {
+  const int tid = threadIdx.x;
+  const int slot = P.row_slot[row];
+  const int len = min(P.slot_len[slot], P.hist_cap);
+  const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+  const long long base = static_cast<long long>(slot) * P.hist_cap;
+  const int nsl = (P.V + kWS - 1) / kWS;   // slices of the row
+  unsigned* cnt = S.lp;                    // scratch counters, one per slice
+  for (int i = tid; i < nsl; i += kT) cnt[i] = 0u;
+  __syncthreads();
+  for (int h = tid; h < len; h += kT) {
+    const int tok = P.hist_tok[base + h];
+    if (P.hist_cnt[base + h] > 0 && tok >= 0 && tok < P.V) atomicAdd(&cnt[tok / kWS], 1u);
+  }
+  __syncthreads();
+  int total;
+  const int v = tid < nsl ? static_cast<int>(cnt[tid]) : 0;   // nsl <= kT
+  const int off = rscan_i(v, S, ph, &total);
+  // slices past the row end (padding of the last round) get empty buckets
+  for (int i = tid; i <= kMaxRounds * kNW; i += kT) S.poff[i] = static_cast<uint16_t>(min(i < nsl ? off : total, kPenCap));
+  if (tid < nsl) cnt[tid] = static_cast<unsigned>(off);
+  if (tid == 0) S.pen_ok = total <= kPenCap;
+  __syncthreads();
+  if (total <= kPenCap) {
+    for (int h = tid; h < len; h += kT) {
+      const int tok = P.hist_tok[base + h];
+      const int c = P.hist_cnt[base + h];
+      if (c > 0 && tok >= 0 && tok < P.V) {
+        const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(c, rf);
+        S.pent[atomicAdd(&cnt[tok / kWS], 1u)] = make_uint2(static_cast<unsigned>(tok % kWS), __float_as_uint(m));
+      }
+    }
+  }
+  __syncthreads();
 }
 
 // Two 16-bit raws -> two order-preserving keys (key16 on each half): prmt
@@ -279,26 +335,35 @@ __device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], 
 // entries e0 .. e0+15 of the row read from global memory with the
 // repetition-penalty patch applied (NaN past the row end)
 template <int DT>
-__device__ void load16(const KParams& P, int row, int e0, float (&yv)[kEPT]) {
+__device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
   const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
-  if (P.row_slot) {
-    const int slot = P.row_slot[row];
-    if (slot >= 0 && slot < P.num_slots) {
-      const int len = min(P.slot_len[slot], P.hist_cap);
-      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
-      const long long hb = static_cast<long long>(slot) * P.hist_cap;
-      for (int h = 0; h < len; ++h) {
-        const int li = P.hist_tok[hb + h] - e0;
-        const int cn = P.hist_cnt[hb + h];
-        if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
-        const float m = P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf);
+  if (!row_has_penalty(P, row)) return;
+  auto patch = [&](int li, float m) {
 #pragma unroll
-        for (int j = 0; j < kEPT; ++j)
-          if (j == li) yv[j] = DType<DT>::round(__fdiv_rn(yv[j], m));
-      }
+    for (int j = 0; j < kEPT; ++j)
+      if (j == li) yv[j] = DType<DT>::round(__fdiv_rn(yv[j], m));
+  };
+  if (S.pen_ok) {
+    // entries e0 .. e0+15 lie in one slice: its bucket of the history
+    const int sl = e0 / kWS, o0 = e0 % kWS;
+    for (int i = S.poff[sl]; i < S.poff[sl + 1]; ++i) {
+      const uint2 e = S.pent[i];
+      const int li = static_cast<int>(e.x) - o0;
+      if (li >= 0 && li < kEPT) patch(li, __uint_as_float(e.y));
     }
+    return;
+  }
+  const int slot = P.row_slot[row];
+  const int len = min(P.slot_len[slot], P.hist_cap);
+  const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+  const long long hb = static_cast<long long>(slot) * P.hist_cap;
+  for (int h = 0; h < len; ++h) {
+    const int li = P.hist_tok[hb + h] - e0;
+    const int cn = P.hist_cnt[hb + h];
+    if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
+    patch(li, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf));
   }
 }
 
@@ -348,7 +413,7 @@ __device__ void stream_row(const KParams& P, RSmem& S, int row, int r0, int r1, 
     // round r - 1, whose stage the next copy reuses
     __syncwarp();
     uint4* st = wst + (r % kStages) * kWV;
-    if (r >= rc) complete_slice<DT>(P, st, row, r, pen);
+    if (r >= rc) complete_slice<DT>(P, S, st, row, r, pen);
     uint32_t raw[8], w[8];
     round_load(st, raw, w);
     if (r + kStages - 1 < r1) issue(r + kStages - 1);
@@ -866,6 +931,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     int fill = 0;
     bool overflow = (N == 0);
 
+    if (row_has_penalty(P, row)) bucket_penalties<DT>(P, S, row, ph);
     uint32_t kcut = 0u;       // mass rows: warps whose keys all lie below skip their masses
     const uint32_t kinf = C::from_val(INFINITY), kninf = C::from_val(-INFINITY);
 
@@ -1022,7 +1088,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       // (fetching them for every thread ahead of the barrier measured slower)
       const int e0 = bround * kRound + kEPT * tid;
       float yv[kEPT];
-      load16<DT>(P, row, e0, yv);
+      load16<DT>(P, S, row, e0, yv);
 #pragma unroll
       for (int j = 0; j < kEPT; ++j)
         if (firstc == 0xFFFFFFFFu && e0 + j < P.V && C::from_val(yv[j]) == kmax) firstc = static_cast<unsigned>(e0 + j);
@@ -1329,7 +1395,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
             float ls = 0.f;
             int lastj = -1;
             float yv[kEPT];
-            load16<DT>(P, row, e0, yv);
+            load16<DT>(P, S, row, e0, yv);
 #pragma unroll
             for (int j = 0; j < kEPT; ++j) {
               const int i = e0 + j;
