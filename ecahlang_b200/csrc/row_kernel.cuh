@@ -232,7 +232,7 @@ __device__ void complete_slice(const KParams& P, const RSmem& S, uint4* st, int 
       const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
       const long long base = static_cast<long long>(slot) * P.hist_cap;
       for (int h = lane; h < len; h += 32) {
-        const int li = P.hist_tok[base + h] - e0;
+        const int li = P.hist_tok[base + h] - P.vocab_offset - e0;
         const int cnt = P.hist_cnt[base + h];
         if (cnt <= 0 || li < 0 || li >= n) continue;
         const float x = Dt::to_f32(raw[li]);
@@ -260,7 +260,7 @@ __device__ void bucket_penalties(const KParams& P, RSmem& S, int row, int& ph) {
   for (int i = tid; i < nsl; i += kT) cnt[i] = 0u;
   __syncthreads();
   for (int h = tid; h < len; h += kT) {
-    const int tok = P.hist_tok[base + h];
+    const int tok = P.hist_tok[base + h] - P.vocab_offset;
     if (P.hist_cnt[base + h] > 0 && tok >= 0 && tok < P.V) atomicAdd(&cnt[tok / kWS], 1u);
   }
   __syncthreads();
@@ -274,7 +274,7 @@ __device__ void bucket_penalties(const KParams& P, RSmem& S, int row, int& ph) {
   __syncthreads();
   if (total <= kPenCap) {
     for (int h = tid; h < len; h += kT) {
-      const int tok = P.hist_tok[base + h];
+      const int tok = P.hist_tok[base + h] - P.vocab_offset;
       const int c = P.hist_cnt[base + h];
       if (c > 0 && tok >= 0 && tok < P.V) {
         const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(c, rf);
@@ -360,7 +360,7 @@ __device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float 
   const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
   const long long hb = static_cast<long long>(slot) * P.hist_cap;
   for (int h = 0; h < len; ++h) {
-    const int li = P.hist_tok[hb + h] - e0;
+    const int li = P.hist_tok[hb + h] - P.vocab_offset - e0;
     const int cn = P.hist_cnt[hb + h];
     if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
     patch(li, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf));
@@ -897,9 +897,144 @@ __device__ __forceinline__ float seg_mass(const RSmem& S, int s, int nseg, float
   return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmaf_rn(-M, kLog2e, S.sq[s]))) : 0.f;
 }
 
+// ------------------------------------------------------------ selection over the finish
+// Among the finishing histogram's bins (bin b: key kmax - b, four per
+// thread), the first whose running count reaches n; INT_MAX when the total
+// stays below n.  *tot = the histogram's total.  Every thread gets the result.
+__device__ __forceinline__ unsigned cnth_select(const unsigned* cnth, int n, RSmem& S, int& ph, int* tot) {
+  const int tid = threadIdx.x;
+  unsigned c4 = 0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) c4 += cnth[tid * 4 + j];
+  const int ex = rscan_i(static_cast<int>(c4), S, ph, tot);
+  int mine = INT_MAX;
+  if (static_cast<unsigned>(ex) < static_cast<unsigned>(n) && static_cast<unsigned>(ex) + c4 >= static_cast<unsigned>(n)) {
+    unsigned acc = static_cast<unsigned>(ex);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const unsigned v = cnth[tid * 4 + j];
+      if (mine == INT_MAX && acc + v >= static_cast<unsigned>(n)) mine = tid * 4 + j;
+      acc += v;
+    }
+  }
+  return rmin_u(static_cast<unsigned>(mine), S, ph);
+}
+
+// The k-th largest key of the row (1 <= k <= its length) by a two-digit
+// (8 | 8 bit) radix select over two re-streams.  Every thread gets it.
+template <int DT>
+__device__ uint32_t radix_kth(const KParams& P, RSmem& S, int row, int R, unsigned k) {
+  const uint32_t lane = threadIdx.x & 31;
+  lp_zero(S);
+  stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j)
+      if (j < nv) atomicAdd(&S.lp[((ECAH_RKEY(w, j) >> 8) << 5) | lane], 1u);
+  });
+  lp_reduce(S);
+  unsigned above;
+  const int hb = h256_select_desc(S, k, &above);
+  lp_zero(S);
+  stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j) {
+      const uint32_t key = ECAH_RKEY(w, j);
+      if (j < nv && static_cast<int>(key >> 8) == hb) atomicAdd(&S.lp[((key & 255u) << 5) | lane], 1u);
+    }
+  });
+  lp_reduce(S);
+  unsigned ab2;
+  const int lb = h256_select_desc(S, k - above, &ab2);
+  return (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(lb);
+}
+
+// ------------------------------------------------ vocabulary-parallel local step
+// After the stream of a slice (P.V entries, first global id P.vocab_offset):
+// the slice's k-th largest key kth -- exact, from the per-key counts of the
+// candidates, which hold every entry with key >= F, or by radix select when
+// kth lies below F -- and every entry with key >= kth (ties included) in
+// vocab order as (key << 32 | global id): the first cand_cap of them, and
+// their count.
+template <int DT>
+__device__ void vp_emit(const KParams& P, RSmem& S, int row, int R, int k, uint32_t kmax, uint32_t F, int fill,
+                        bool cand, int& ph) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned long long* dst = P.vp_cand + static_cast<long long>(row) * P.cand_cap;
+  const unsigned gofs = static_cast<unsigned>(P.vocab_offset);
+  if (cand) {
+    unsigned* cnth = reinterpret_cast<unsigned*>(&S.stage[0][0]) + kCntOff;   // zeroed before the gather
+    if (kmax >= static_cast<uint32_t>(kHB) && F < kmax - static_cast<uint32_t>(kHB - 1))
+      F = kmax - static_cast<uint32_t>(kHB - 1);
+    for (int i = tid; i < fill; i += kT) {
+      const unsigned key = gkey(S)[i];
+      if (key >= F) atomicAdd(&cnth[kmax - key], 1u);
+    }
+    __syncthreads();
+    int tot;
+    const unsigned b = cnth_select(cnth, k, S, ph, &tot);
+    if (b != static_cast<unsigned>(INT_MAX) && kmax - b >= F) {
+      const uint32_t kth = kmax - b;
+      // the candidates in vocab order: 8 consecutive per thread
+      const int b0 = tid * 8;
+      unsigned m8 = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (b0 + j < fill && gkey(S)[b0 + j] >= kth) m8 |= 1u << j;
+      int total;
+      int o = rscan_i(__popc(m8), S, ph, &total);
+      for (; m8; m8 &= m8 - 1u) {
+        const int i = b0 + __ffs(m8) - 1;
+        if (o < P.cand_cap) dst[o] = (static_cast<unsigned long long>(gkey(S)[i]) << 32) | (gofs + gidx(S)[i]);
+        ++o;
+      }
+      if (tid == 0) P.vp_count[row] = total;
+      return;
+    }
+  }
+  // kth below the candidates: radix select, then per (round, warp) segment
+  // the count of entries >= kth, their offsets, and the entries
+  const uint32_t kth = radix_kth<DT>(P, S, row, R, static_cast<unsigned>(k));
+  int* segc = reinterpret_cast<int*>(S.ss);
+  stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j) c += (j < nv && ECAH_RKEY(w, j) >= kth) ? 1 : 0;
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if (lane == 0) segc[r * kNW + warp] = c;
+  });
+  int total;
+  const int off = rscan_i(tid < R * kNW ? segc[tid] : 0, S, ph, &total);
+  if (tid < R * kNW) segc[tid] = off;
+  stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+    unsigned m = 0u;
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j)
+      if (j < nv && ECAH_RKEY(w, j) >= kth) m |= 1u << j;
+    const int c = __popc(m);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int o = segc[r * kNW + warp] + incl - c;
+    const unsigned e0 = gofs + static_cast<unsigned>(r * kRound + kEPT * tid);
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j) {
+      if ((m >> j) & 1u) {
+        if (o < P.cand_cap) dst[o] = (static_cast<unsigned long long>(ECAH_RKEY(w, j)) << 32) | (e0 + j);
+        ++o;
+      }
+    }
+  });
+  if (tid == 0) P.vp_count[row] = total;
+}
+
 // ------------------------------------------------------------ the kernel
-template <int DT, bool SPLIT>
-__global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
+// One body for the sampler (VPL false) and for the vocabulary-parallel local
+// step (VPL: candidates only, then vp_emit).
+template <int DT, bool SPLIT, bool VPL>
+__device__ __forceinline__ void row_body(const KParams& P) {
   using C = Codec<DT, 16>;
   extern __shared__ __align__(16) unsigned char dsm[];
   RSmem& S = *reinterpret_cast<RSmem*>(dsm);
@@ -920,9 +1055,20 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     const bool sampled = T > 0.f;
     const bool t1 = (T == 1.0f);
     const float rT = __frcp_rn(T);
-    const int N = !sampled ? 0 : (topk ? (k_eff <= kMaxN ? k_eff : 0) : (topp ? kDenseN : 0));
-    const bool mass_all = sampled && !topk;        // S over the whole row
-    const bool segs = mass_all && !topp;           // draw from segment sums
+    int N = !sampled ? 0 : (topk ? (k_eff <= kMaxN ? k_eff : 0) : (topp ? kDenseN : 0));
+    if constexpr (VPL) {
+      // k = top_k, the whole vocabulary when off, 1 for greedy rows; rows
+      // whose list cannot hold k entries get count k and no list (the merge
+      // refuses them)
+      const long long kr = !sampled ? 1 : ((kk <= 0 || kk >= P.vocab_total) ? P.vocab_total : kk);
+      N = static_cast<int>(min(kr, static_cast<long long>(P.V)));
+      if (N > P.cand_cap) {
+        if (tid == 0) P.vp_count[row] = N;
+        continue;
+      }
+    }
+    const bool mass_all = !VPL && sampled && !topk;   // S over the whole row
+    const bool segs = mass_all && !topp;              // draw from segment sums
 
     // running state
     unsigned best = 0u;       // thread max key
@@ -988,7 +1134,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
           // largest key is never below it either); top-p rows scale N to the
           // round's share of the row, so about N entries pass in all.
           const int n0 = round_len(P.V, r0);
-          const int N0 = topk ? N : max(1, static_cast<int>((static_cast<long long>(N) * n0 + P.V - 1) / P.V));
+          const int N0 = (VPL || topk) ? N : max(1, static_cast<int>((static_cast<long long>(N) * n0 + P.V - 1) / P.V));
           if (tid < 256) S.h256[tid] = 0u;
           __syncthreads();
           const uint32_t d0 = k0 - tm;
@@ -1077,6 +1223,11 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     // ------------------------------------------------ row max and greedy
     unsigned kmax, fmax;
     rmax2_u(best, N > 0 ? f : 0u, S, ph, &kmax, &fmax);
+    if constexpr (VPL) {
+      vp_emit<DT>(P, S, row, R, N, kmax, fmax, fill, cand, ph);
+      __syncthreads();  // shared state is reused by the next row
+      continue;
+    }
     if (N > 0) f = fmax;
     unsigned firstc = 0xFFFFFFFFu;
     if (cand) {
@@ -1151,24 +1302,8 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
         const int Bmax = static_cast<int>(kmax - F);
         // top-k: the k-th largest key among the candidates
         if (topk) {
-          // threads own 4 consecutive bins; running counts in bin order
-          unsigned c4 = 0u;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) c4 += cnth[tid * 4 + j];
           int tot;
-          const int ex = rscan_i(static_cast<int>(c4), S, ph, &tot);
-          int mine = INT_MAX;
-          if (static_cast<unsigned>(ex) < static_cast<unsigned>(k_eff) &&
-              static_cast<unsigned>(ex) + c4 >= static_cast<unsigned>(k_eff)) {
-            unsigned acc = static_cast<unsigned>(ex);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const unsigned v = cnth[tid * 4 + j];
-              if (mine == INT_MAX && acc + v >= static_cast<unsigned>(k_eff)) mine = tid * 4 + j;
-              acc += v;
-            }
-          }
-          const unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+          const unsigned bsel = cnth_select(cnth, k_eff, S, ph, &tot);
           if (tot < k_eff || bsel == static_cast<unsigned>(INT_MAX)) {
             fast = false;
           } else {
@@ -1229,31 +1364,7 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
       if (!fast) {
         // ---------------------------------- fallback: radix select by re-streaming
         key_lo_k = 0u;
-        if (topk) {
-          lp_zero(S);
-          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
-#pragma unroll
-            for (int j = 0; j < kEPT; ++j)
-              if (j < nv) atomicAdd(&S.lp[((ECAH_RKEY(w, j) >> 8) << 5) | static_cast<uint32_t>(lane)], 1u);
-          });
-          lp_reduce(S);
-          unsigned above;
-          const int hb = h256_select_desc(S, static_cast<unsigned>(k_eff), &above);
-          lp_zero(S);
-          stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
-#pragma unroll
-            for (int j = 0; j < kEPT; ++j) {
-              const uint32_t key = ECAH_RKEY(w, j);
-              if (j < nv && static_cast<int>(key >> 8) == hb) atomicAdd(&S.lp[((key & 255u) << 5) | static_cast<uint32_t>(lane)], 1u);
-            }
-          });
-          lp_reduce(S);
-          unsigned ab2;
-          const int lb = h256_select_desc(S, static_cast<unsigned>(k_eff) - above, &ab2);
-          if (tid == 0) S.ib[0] = static_cast<int>(tie_floor<DT, 16>((static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(lb), T));
-          __syncthreads();
-          key_lo_k = static_cast<uint32_t>(S.ib[0]);
-        }
+        if (topk) key_lo_k = tie_floor<DT, 16>(radix_kth<DT>(P, S, row, R, static_cast<unsigned>(k_eff)), T);
         key_lo = key_lo_k;
         if (topp) {
           const uint32_t klo = max(key_lo_k, key_cut);
@@ -1473,6 +1584,18 @@ __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant
     }
     __syncthreads();  // shared state is reused by the next row
   }
+}
+
+template <int DT, bool SPLIT>
+__global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
+  row_body<DT, SPLIT, false>(P);
+}
+
+// Vocabulary-parallel local step: per row of the slice, the entries at or
+// above the slice's k-th largest key (vp_emit).  P.V is the slice length.
+template <int DT>
+__global__ void __launch_bounds__(kT, 1) vp_local_row_kernel(const __grid_constant__ KParams P) {
+  row_body<DT, false, true>(P);
 }
 
 #undef ECAH_RKEY

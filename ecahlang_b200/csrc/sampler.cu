@@ -317,60 +317,77 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   return e == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
 
-static int vp_params(const ecah_vp_args* a, vp::VParams* P) {
+// the checks both vocab-parallel entry points share
+static int vp_check(const ecah_vp_args* a) {
   if (!a) return ECAH_ERR_NULL;
   if (a->abi_version != ECAH_SAMPLER_ABI_VERSION) return ECAH_ERR_ABI;
   if (!k16_dtype(a->dtype)) return ECAH_ERR_DTYPE;
-  if (a->batch < 0 || a->vocab < 1 || a->vocab_local < 1 || a->vocab_local > vp::kMaxLocal || a->vocab_offset < 0 ||
+  if (a->batch < 0 || a->vocab < 1 || a->vocab_local < 1 || a->vocab_local > rk::kMaxRounds * rk::kRound ||
+      a->vocab_offset < 0 ||
       static_cast<long long>(a->vocab_offset) + a->vocab_local > a->vocab || a->row_stride < a->vocab_local ||
       a->cand_cap < 1 || a->world < 1 || a->world > 64 || static_cast<long long>(a->world) * a->cand_cap > vp::kMaxMerged)
     return ECAH_ERR_SHAPE;
   if (a->batch > 0 && (!a->temperature || !a->top_k || !a->top_p)) return ECAH_ERR_NULL;
-  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
-  *P = vp::VParams{};
-  P->logits = a->logits; P->row_stride = a->row_stride; P->B = a->batch; P->Vl = a->vocab_local; P->V = a->vocab;
-  P->offset = a->vocab_offset; P->temperature = a->temperature; P->top_k = a->top_k; P->top_p = a->top_p;
-  P->rep_factor = a->rep_factor; P->row_slot = a->row_slot; P->slot_len = a->slot_len; P->hist_tok = a->hist_tok;
-  P->hist_cnt = a->hist_cnt; P->hist_mval = a->hist_mval; P->hist_cap = a->hist_cap; P->num_slots = a->num_slots;
-  P->cap = a->cand_cap; P->cand = reinterpret_cast<unsigned long long*>(a->cand); P->count = a->cand_count;
-  P->world = a->world; P->all_cand = reinterpret_cast<const unsigned long long*>(a->all_cand);
-  P->all_count = a->all_count; P->uniforms = a->uniforms;
-  P->philox_state = reinterpret_cast<unsigned long long*>(a->philox_state);
-  P->done_counter = reinterpret_cast<unsigned*>(a->workspace); P->out = a->out; P->row_stats = a->row_stats;
-  P->vec_ok = (reinterpret_cast<uintptr_t>(a->logits) % 16 == 0) && ((a->row_stride * 2) % 16 == 0);
   return ECAH_OK;
 }
 
 int ecah_vp_local(const ecah_vp_args* a, void* stream) {
-  vp::VParams P;
-  const int st = vp_params(a, &P);
+  const int st = vp_check(a);
   if (st != ECAH_OK) return st;
   if (a->batch == 0) return ECAH_OK;
   if (!a->logits || !a->cand || !a->cand_count) return ECAH_ERR_NULL;
-  const int smem = static_cast<int>(sizeof(vp::LSmem));
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (a->dtype == ECAH_DTYPE_F16) {
-    if (cudaFuncSetAttribute(vp::vp_local_kernel<ECAH_DTYPE_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return ECAH_ERR_LAUNCH;
-    vp::vp_local_kernel<ECAH_DTYPE_F16><<<a->batch, vp::kLT, smem, s>>>(P);
-  } else {
-    if (cudaFuncSetAttribute(vp::vp_local_kernel<ECAH_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return ECAH_ERR_LAUNCH;
-    vp::vp_local_kernel<ECAH_DTYPE_BF16><<<a->batch, vp::kLT, smem, s>>>(P);
-  }
+  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
+  // the row kernel's stream and candidates over the slice (P.V = its length)
+  KParams P = {};
+  P.logits = a->logits;
+  P.row_stride = a->row_stride;
+  P.B = a->batch;
+  P.V = a->vocab_local;
+  P.temperature = a->temperature;
+  P.top_k = a->top_k;
+  P.top_p = a->top_p;
+  P.rep_factor = a->rep_factor;
+  P.row_slot = a->row_slot;
+  P.slot_len = a->slot_len;
+  P.hist_tok = a->hist_tok;
+  P.hist_cnt = a->hist_cnt;
+  P.hist_mval = a->hist_mval;
+  P.hist_cap = a->hist_cap;
+  P.num_slots = a->num_slots;
+  P.vec_ok = (reinterpret_cast<uintptr_t>(a->logits) % 16 == 0) && ((a->row_stride * 2) % 16 == 0);
+  P.vocab_offset = a->vocab_offset;
+  P.vocab_total = a->vocab;
+  P.cand_cap = a->cand_cap;
+  P.vp_cand = reinterpret_cast<unsigned long long*>(a->cand);
+  P.vp_count = a->cand_count;
+  const int smem = static_cast<int>(sizeof(rk::RSmem));
+  const int sms = device_sms();
+  if (sms <= 0) return ECAH_ERR_LAUNCH;
+  const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
+  KernelFn fn = a->dtype == ECAH_DTYPE_F16 ? rk::vp_local_row_kernel<ECAH_DTYPE_F16> : rk::vp_local_row_kernel<ECAH_DTYPE_BF16>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
+  fn<<<grid, rk::kT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
   return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
 
 int ecah_vp_merge(const ecah_vp_args* a, void* stream) {
-  vp::VParams P;
-  const int st = vp_params(a, &P);
+  const int st = vp_check(a);
   if (st != ECAH_OK) return st;
   if (a->batch == 0) return ECAH_OK;
   if (!a->all_cand || !a->all_count || !a->out) return ECAH_ERR_NULL;
   if (!a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
   if (!a->workspace || a->workspace_bytes < kMinWorkspace) return ECAH_ERR_WORKSPACE;
+  vp::VParams P = {};
+  P.B = a->batch; P.V = a->vocab;
+  P.temperature = a->temperature; P.top_k = a->top_k; P.top_p = a->top_p;
+  P.cap = a->cand_cap; P.world = a->world;
+  P.all_cand = reinterpret_cast<const unsigned long long*>(a->all_cand);
+  P.all_count = a->all_count;
+  P.uniforms = a->uniforms;
+  P.philox_state = reinterpret_cast<unsigned long long*>(a->philox_state);
+  P.done_counter = reinterpret_cast<unsigned*>(a->workspace);
+  P.out = a->out;
+  P.row_stats = a->row_stats;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (a->dtype == ECAH_DTYPE_F16) vp::vp_merge_kernel<ECAH_DTYPE_F16><<<a->batch, vp::kMT, 0, s>>>(P);
   else vp::vp_merge_kernel<ECAH_DTYPE_BF16><<<a->batch, vp::kMT, 0, s>>>(P);

@@ -84,6 +84,12 @@ struct KParams {
   void* part_hdr;                   // [B, parts] per-part results
   unsigned long long* part_cand;    // [B, parts, kCB] candidates: key << 32 | row index
   float2* part_seg;                 // [B, 32 rounds x 32 warps] segment (mass, reference)
+  // vocabulary-parallel local step on the row kernel: V is the slice length
+  int vocab_offset;                 // global id of the slice's first entry (0 otherwise)
+  int vocab_total;                  // the whole vocabulary
+  int cand_cap;                     // list entries per row
+  unsigned long long* vp_cand;      // [B, cand_cap] key << 32 | global id, vocab order
+  int* vp_count;                    // [B] entries at or above the k-th largest key
 };
 
 constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private

@@ -1,12 +1,12 @@
 // Vocab-parallel sampling (fp16/bf16 logits): every rank holds a contiguous
 // slice [vocab_offset, vocab_offset + vocab_local) of each row.
 //
-// vp_local_kernel (one CTA per row) keeps the slice in shared memory, applies
-// the repetition-penalty patch of the row's history tokens that fall in the
-// slice, finds the slice's k-th largest key (k = top_k, 1 for greedy rows)
-// with a two-digit (8 | 8 bit) radix select, and writes every slice entry
-// whose key is >= that key -- ties included -- in vocab order as
-// (key << 32 | global id), up to cand_cap of them, plus their count.
+// The local step is the row kernel's stream over the slice
+// (rk::vp_local_row_kernel): repetition-penalty patch of the row's history
+// tokens that fall in the slice, the slice's k-th largest key (k = top_k, 1
+// for greedy rows) and every slice entry whose key is >= that key -- ties
+// included -- in vocab order as (key << 32 | global id), up to cand_cap of
+// them, plus their count.
 //
 // Because the row's k-th largest key is >= every slice's k-th largest key,
 // the union of the slices' lists holds every entry of the row's top-k set.
@@ -23,166 +23,27 @@
 namespace ecah {
 namespace vp {
 
-constexpr int kLT = 512;                 // threads of the local kernel
-constexpr int kLW = kLT / 32;
-constexpr int kMaxLocal = 65536;         // slice entries held in shared memory
 constexpr int kMT = 256;                 // threads of the merge kernel
 constexpr int kMW = kMT / 32;
 constexpr int kMaxMerged = 2048;         // world * cand_cap entries per row, at most
 constexpr int kWin = 4096;               // merge histogram: keys below the row max
 
+// what the merge reads (the local step runs on the row kernel's KParams)
 struct VParams {
-  const void* logits;
-  long long row_stride;
-  int B, Vl, V, offset;
+  int B, V;
   const float* temperature;
   const int* top_k;
   const float* top_p;
-  const float* rep_factor;
-  const int* row_slot;
-  const int* slot_len;
-  const int* hist_tok;
-  const int* hist_cnt;
-  const float* hist_mval;
-  int hist_cap, num_slots;
   int cap;                                // candidates per row and rank
-  unsigned long long* cand;               // [B, cap] local lists
-  int* count;                             // [B] local counts (> cap: truncated)
   int world;
   const unsigned long long* all_cand;     // [world, B, cap]
-  const int* all_count;                   // [world, B]
+  const int* all_count;                   // [world, B] (> cap: truncated)
   const float* uniforms;
   unsigned long long* philox_state;
   unsigned* done_counter;
   int* out;
   float* row_stats;
-  int vec_ok;
 };
-
-// ------------------------------------------------------------ local step
-struct LSmem {
-  uint16_t raw[kMaxLocal];   // the slice (raw logits, penalised)
-  unsigned lp[256 * 32];     // lane-private 256-bin histogram
-  unsigned h[256];
-  int wsum[kLW];
-  int ib[4];
-};
-
-template <int DT>
-__global__ void __launch_bounds__(kLT) vp_local_kernel(const __grid_constant__ VParams P) {
-  using Dt = DType<DT>;
-  extern __shared__ __align__(16) unsigned char dsm[];
-  LSmem& S = *reinterpret_cast<LSmem*>(dsm);
-  const int row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = P.Vl;
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
-
-  // load the slice
-  int done = 0;
-  if (P.vec_ok) {
-    const int nfull = n >> 3;
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* d4 = reinterpret_cast<uint4*>(S.raw);
-    for (int v = tid; v < nfull; v += kLT) cp_async16(d4 + v, s4 + v);
-    done = nfull << 3;
-  }
-  for (int i = done + tid; i < n; i += kLT) S.raw[i] = src[i];
-  cp_async_wait_all();
-  __syncthreads();
-  if (P.row_slot) {
-    const int slot = P.row_slot[row];
-    if (slot >= 0 && slot < P.num_slots) {
-      const int len = min(P.slot_len[slot], P.hist_cap);
-      const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
-      const long long base = static_cast<long long>(slot) * P.hist_cap;
-      for (int h = tid; h < len; h += kLT) {
-        const int li = P.hist_tok[base + h] - P.offset;
-        const int cnt = P.hist_cnt[base + h];
-        if (cnt <= 0 || li < 0 || li >= n) continue;
-        const float x = Dt::to_f32(S.raw[li]);
-        const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
-        S.raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
-      }
-    }
-    __syncthreads();
-  }
-
-  const float T = P.temperature[row];
-  const int kk = P.top_k[row];
-  // rows without top-k keep every entry (they fit only in small slices)
-  const long long k_row = (!(T > 0.f)) ? 1 : ((kk <= 0 || kk >= P.V) ? static_cast<long long>(P.V) : kk);
-  const unsigned k = static_cast<unsigned>(min(k_row, static_cast<long long>(n)));
-
-  // k-th largest key of the slice: high byte, then low byte
-  for (int i = tid; i < 256 * 32; i += kLT) S.lp[i] = 0u;
-  __syncthreads();
-  for (int i = tid; i < n; i += kLT) atomicAdd(&S.lp[((key16(S.raw[i]) >> 8) << 5) | lane], 1u);
-  __syncthreads();
-  if (tid < 256) {
-    unsigned acc = 0u;
-    for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
-    S.h[tid] = acc;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    int b; unsigned above;
-    warp_select_seq<unsigned, 256, true>(S.h, k, &b, &above);
-    if (lane == 0) { S.ib[0] = b; S.ib[1] = static_cast<int>(above); }
-  }
-  __syncthreads();
-  const int hb = S.ib[0];
-  const unsigned krem = k - static_cast<unsigned>(S.ib[1]);
-  for (int i = tid; i < 256 * 32; i += kLT) S.lp[i] = 0u;
-  __syncthreads();
-  for (int i = tid; i < n; i += kLT) {
-    const uint32_t key = key16(S.raw[i]);
-    if (static_cast<int>(key >> 8) == hb) atomicAdd(&S.lp[((key & 255u) << 5) | lane], 1u);
-  }
-  __syncthreads();
-  if (tid < 256) {
-    unsigned acc = 0u;
-    for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
-    S.h[tid] = acc;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    int b; unsigned above;
-    warp_select_seq<unsigned, 256, true>(S.h, krem, &b, &above);
-    if (lane == 0) S.ib[2] = static_cast<int>((static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(b));
-  }
-  __syncthreads();
-  const uint32_t kth = static_cast<uint32_t>(S.ib[2]);
-
-  // entries >= kth in vocab order: thread t owns a contiguous stretch
-  const int per = (n + kLT - 1) / kLT;
-  const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
-  int cnt = 0;
-  for (int i = i0; i < i1; ++i) cnt += (key16(S.raw[i]) >= kth) ? 1 : 0;
-  int incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  if (lane == 31) S.wsum[warp] = incl;
-  __syncthreads();
-  int base = 0, total = 0;
-  for (int w = 0; w < kLW; ++w) {
-    if (w < warp) base += S.wsum[w];
-    total += S.wsum[w];
-  }
-  int o = base + incl - cnt;
-  unsigned long long* dst = P.cand + static_cast<long long>(row) * P.cap;
-  for (int i = i0; i < i1 && o < P.cap; ++i) {
-    const uint32_t key = key16(S.raw[i]);
-    if (key >= kth) {
-      dst[o] = (static_cast<unsigned long long>(key) << 32) | static_cast<unsigned>(P.offset + i);
-      ++o;
-    }
-  }
-  if (tid == 0) P.count[row] = total;
-}
 
 // ------------------------------------------------------------ merge step
 struct MSmem {
@@ -261,7 +122,10 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
   const unsigned first = mblock_min(fid, S.ured);
   const float ymax = C::value(kmax);
   const float M = __fdiv_rn(ymax, T);
-  const bool greedy = !(T > 0.f) || !isfinite(M);
+  // a truncated sampled row is refused whatever its lists hold (a rank whose
+  // k exceeds cand_cap writes no list); greedy rows need only each rank's
+  // first entries, which a truncated list keeps
+  const bool greedy = !(T > 0.f) || (!truncated && !isfinite(M));
   int result = static_cast<int>(first == 0xFFFFFFFFu ? 0u : first);
   float Z = 1.0f;
   uint32_t key_lo_k = kmax, key_lo = kmax;

@@ -24,7 +24,7 @@ from typing import Dict, Iterable, Optional, Sequence
 import numpy as np
 import torch
 
-from .sampler import PenaltyState, launch, new_philox_state, new_workspace, repetition_factor
+from .sampler import PenaltyState, launch, new_philox_state, new_workspace, repetition_factor, resolve_device
 
 
 def _pinned(t: torch.Tensor) -> torch.Tensor:
@@ -39,7 +39,7 @@ class SamplingManager:
         self.vocab_size = vocab_size
         self.seq_lens = max(seq_lens, 128)                      # manager.py:31
         self.dtype = dtype
-        self.device = torch.device(device)
+        self.device = resolve_device(device)
         # replaces mask_penalty = ones(seq_lens, V) (manager.py:36)
         self.penalty = PenaltyState(self.seq_lens, history_capacity, dtype, self.device)
         self.free_seq_lens = list(range(self.seq_lens))         # manager.py:57

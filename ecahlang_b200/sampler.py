@@ -20,6 +20,15 @@ from ._abi import SamplerArgs, check, lib
 _DTYPES = {torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16, torch.float32: _abi.DTYPE_F32}
 
 
+def resolve_device(device) -> torch.device:
+    """torch.device with an explicit index ("cuda" -> the current CUDA
+    device), so it compares equal to the device of the tensors made on it."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None and torch.cuda.is_available():
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -210,7 +219,7 @@ class Sampler:
 
     def __init__(self, max_batch: int, vocab: int, dtype: torch.dtype, device="cuda", seed: int = 0):
         self.vocab, self.dtype = vocab, dtype
-        self.device = torch.device(device)
+        self.device = resolve_device(device)
         self.workspace = new_workspace(max_batch, vocab, dtype, self.device)
         self.philox_state = new_philox_state(seed, 0, self.device)
         self.out = torch.zeros(max_batch, dtype=torch.int32, device=self.device)

@@ -21,7 +21,7 @@ import torch
 
 from . import _abi
 from ._abi import VPArgs, check, lib
-from .sampler import PenaltyState, new_philox_state
+from .sampler import PenaltyState, new_philox_state, resolve_device
 
 _DTYPES = {torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16}
 
@@ -61,7 +61,7 @@ class VocabParallelSampler:
         self.vocab, self.world, self.rank, self.dtype = vocab, world, rank, dtype
         self.offset, self.nlocal = split_vocab(vocab, world, rank)
         self.cap = cand_cap
-        dev = torch.device(device)
+        dev = resolve_device(device)
         self.device = dev
         self.cand = torch.zeros(max_batch, cand_cap, dtype=torch.int64, device=dev)
         self.count = torch.zeros(max_batch, dtype=torch.int32, device=dev)

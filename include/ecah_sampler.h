@@ -171,11 +171,12 @@ ECAH_API size_t ecah_sampler_noalloc_scratch_bytes(void);
  * logits.  ecah_vp_local writes, per row, every local entry whose key is >=
  * the slice's k-th largest key (ties included; k = top_k, 1 for greedy rows)
  * in vocab order as (key << 32 | global id), at most cand_cap of them, and
- * their count.  The caller all-gathers cand/cand_count over the ranks (rank
- * order) into all_cand/all_count; ecah_vp_merge then draws the same token on
- * every rank (the same uniforms / Philox state on every rank).  Rows need
+ * their count (rows whose k exceeds cand_cap get no list and count = k).
+ * The caller all-gathers cand/cand_count over the ranks (rank order) into
+ * all_cand/all_count; ecah_vp_merge then draws the same token on every rank
+ * (the same uniforms / Philox state on every rank).  Rows need
  * 1 <= top_k <= cand_cap (or T <= 0); rows with top-k off, or whose lists
- * were truncated, get out = -1.  Replaces the whole-row FlashInfer call of
+ * were truncated (count > cand_cap), get out = -1.  Replaces the whole-row FlashInfer call of
  * ecahlang/main.py:377-379 when the LM head is split by vocabulary (ecahLang
  * itself runs on one GPU, ecahlang/env.py:112).
  */
@@ -185,7 +186,7 @@ typedef struct ecah_vp_args {
   int32_t batch;
   int32_t vocab;              /* full vocabulary                                 */
   int32_t vocab_offset;       /* this rank's first column                        */
-  int32_t vocab_local;        /* this rank's columns, 1 .. 65536                 */
+  int32_t vocab_local;        /* this rank's columns, 1 .. 524288                */
   int64_t row_stride;         /* elements between rows of the local slice        */
   const void* logits;         /* [batch, row_stride] local slice                 */
   const float* temperature;   /* [batch]                                         */

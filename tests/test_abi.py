@@ -96,7 +96,8 @@ def test_vocab_parallel_rejects_bad_arguments_without_a_device(L):
     assert L.ecah_vp_local(vp(abi_version=3), None) == 6
     assert L.ecah_vp_local(vp(dtype=2), None) == 2                  # fp32 logits: not supported
     assert L.ecah_vp_local(vp(vocab_offset=600), None) == 3         # slice past the row end
-    assert L.ecah_vp_local(vp(vocab_local=70000, vocab=200000, row_stride=70000), None) == 3
+    assert L.ecah_vp_local(vp(vocab_local=524289, vocab=600000, row_stride=524289), None) == 3  # > 32 rounds
+    assert L.ecah_vp_local(vp(vocab_local=70000, vocab=200000, row_stride=69999), None) == 3  # stride < slice
     assert L.ecah_vp_local(vp(world=16, cand_cap=256), None) == 3   # world * cap > 2048
     assert L.ecah_vp_local(vp(), None) == 1                         # parameter arrays missing
     assert L.ecah_vp_merge(vp(batch=0), None) == 0

@@ -12,7 +12,9 @@ from oracle import sampler_oracle as so
 def local_lists(xf: np.ndarray, top_k: np.ndarray, T: np.ndarray, offset: int, cap: int):
     """Per row of the slice xf [B, local]: every entry at or above the slice's
     k-th largest value (ties included; k = 1 for greedy rows), in vocab order,
-    as global ids; also the untruncated counts."""
+    as global ids; also the untruncated counts.  Values compare as floats
+    (-0.0 == +0.0); ecah_vp_local compares 16-bit keys, where -0.0 sorts
+    below +0.0, so its lists can be shorter by the zeros of the other sign."""
     B, n = xf.shape
     ids = np.full((B, cap), -1, np.int64)
     cnt = np.zeros(B, np.int32)
