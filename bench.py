@@ -293,9 +293,8 @@ def run_native(a):
                          "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke},
-            # one kernel per sampler launch at B >= 32 (one CTA per row), two below
-            # (chunk scan + row finish); no other kernels run in the timed region
-            "gpu_launches": a.steps * (1 if B >= 32 else 2),
+            # one sampler kernel per step; no other kernels run in the timed region
+            "gpu_launches": a.steps,
             "clocks": clk.summary(),
         }
         if ws == 1 and not a.no_cpu_baseline:
@@ -321,8 +320,11 @@ def run_native(a):
 
 def run_vocab_parallel(a):
     """B=512, V=128256 bf16 split by vocabulary over the ranks; a
-    step = local candidates + NCCL all-gather + merge, the same ids on every
-    rank.  Time = max over ranks of CUDA-event time; value = rows/s of the job."""
+    step gives the same ids on every rank.  --exchange peer (default): one
+    fused kernel per rank, lists stored straight into every rank's exchange
+    buffer over NVLink; nccl: local kernel, NCCL all-gather, merge kernel.
+    Steps are replayed from CUDA graphs; time = max over ranks of CUDA-event
+    time; value = rows/s of the job."""
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -339,45 +341,89 @@ def run_vocab_parallel(a):
     bufs = [w.logits[:, off:off + loc].contiguous().to(dev) for _ in range(nbuf)]
     T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
     cap = min(256, 2048 // ws)
-    exch = None if ws > 1 else (lambda c, n, ac, an: (ac[0].copy_(c), an[0].copy_(n)))
+    peer = a.exchange == "peer" and ws > 1
+    if peer:
+        exch = "peer"
+    elif ws > 1:
+        exch = None   # NCCL all-gather
+    else:
+        exch = lambda c, n, ac, an: (ac[0].copy_(c), an[0].copy_(n))
     smp = VocabParallelSampler(B, V, ws, rank, torch.bfloat16, dev, seed=77, cand_cap=cap, exchange=exch)
     stream = torch.cuda.current_stream(dev)
     for i in range(a.warmup):
         smp(bufs[i % nbuf], T, K, P)
+    torch.cuda.synchronize()
+    chunk = min(a.steps, 2 * nbuf)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+
+    def capture(n, fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(n):
+                fn(i)
+        return g
+
+    g_full = capture(chunk, lambda i: smp(bufs[i % nbuf], T, K, P))
+    rem = a.steps % chunk
+    g_rem = capture(rem, lambda i: smp(bufs[i % nbuf], T, K, P)) if rem else None
+    g_full.replay()
     torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for i in range(a.steps):
-            smp(bufs[i % nbuf], T, K, P)
+        for _ in range(a.steps // chunk):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    err = smp.peer.error() if smp.peer is not None else 0
+    # the local kernel alone (the step's HBM pass), on this rank
+    g_loc = capture(chunk, lambda i: smp.local(bufs[i % nbuf], T, K, P))
+    g_loc.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    reps = max(1, min(20, a.steps // chunk))
+    for _ in range(reps):
+        g_loc.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / (reps * chunk)
     if ws > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, ms_local, float(err)], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, ms_local, err = float(t[0].item()), float(t[1].item()), int(t[2].item())
         torch.distributed.barrier()
+    del g_full, g_rem, g_loc
+    smp.close()
+    if ws > 1:
         torch.distributed.destroy_process_group()
     if rank == 0:
         ms_step = ms / a.steps
         peak, peak_kind = _peaks()
         alg = bytes_in   # per rank: its slice of the logits
-        achieved = alg / (ms_step / 1e3) / 1e9
+        achieved = alg / (ms_local / 1e3) / 1e9
+        how = ("fused kernel, lists stored into every rank's buffer over NVLink (CUDA IPC)" if peer else
+               "local kernel + NCCL all_gather + merge kernel" if ws > 1 else "local + merge kernels (1 rank)")
         print(json.dumps({
             "metric": "vocab-parallel sampler rows/sec (configs[3]: B=512, V=128256 bf16, k=64, p=0.9)",
             "value": B / (ms_step / 1e3), "unit": "rows/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
+            "ms_per_step": ms_step, "us_per_step": 1e3 * ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "c4_vocab_parallel B=512 V=128256 bf16", "slice_per_rank": loc,
-                       "cand_cap": cap, "exchange": "NCCL all_gather" if ws > 1 else "none (1 rank)",
-                       "launch": "eager (Python launch per step)"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                         "algorithmic_bytes_per_launch": alg},
-            "gpu_launches": a.steps * 2, "clocks": clk.summary(),
+                       "cand_cap": cap, "exchange": how, "launch": f"CUDA-graph replays of {chunk} steps",
+                       "l2": f"inputs rotate through {nbuf} device copies"},
+            "roofline": {"bound": "hbm", "kernel": "local step (vp_local_row_kernel)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": alg,
+                         "us_per_launch": 1e3 * ms_local},
+            "wait_timeouts": err,
+            "gpu_launches": a.steps * (1 if peer else 2),   # ours; NCCL and copy kernels not counted
+            "clocks": clk.summary(),
         }), flush=True)
 
 
@@ -482,6 +528,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["batch", "vp"], default="batch",
                     help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="vp mode: fused kernel over NVLink peer memory, or NCCL all-gather between kernels")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     if a.impl == "reference":

@@ -23,7 +23,9 @@ STATUS = {0: "ok", 1: "null pointer", 2: "dtype", 3: "shape", 4: "workspace", 5:
 EXPORTS = ("ecah_sampler_abi_version", "ecah_status_string", "ecah_sampler_workspace_bytes",
            "ecah_sampler_launch", "ecah_hist_update", "ecah_philox_uniforms",
            "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes",
-           "ecah_vp_local", "ecah_vp_merge")
+           "ecah_vp_local", "ecah_vp_merge", "ecah_vp_exchange_bytes", "ecah_vp_step",
+           "ecah_vp_ipc_alloc", "ecah_vp_ipc_open", "ecah_vp_ipc_close", "ecah_vp_ipc_free")
+IPC_HANDLE_BYTES = 64
 
 
 class SamplerArgs(ctypes.Structure):
@@ -55,6 +57,11 @@ class VPArgs(ctypes.Structure):
         ("philox_state", c_void_p), ("out", c_void_p), ("row_stats", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
+
+
+class VPPeers(ctypes.Structure):
+    """Mirror of ``struct ecah_vp_peers``."""
+    _fields_ = [("rank", c_int32), ("max_batch", c_int32), ("base", c_void_p), ("timeout_us", c_uint32)]
 
 
 class EcahError(RuntimeError):
@@ -93,6 +100,18 @@ def lib():
         L.ecah_vp_merge.argtypes = [ctypes.POINTER(VPArgs), c_void_p]
         L.ecah_philox_uniforms.restype = c_int32
         L.ecah_philox_uniforms.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_void_p]
+        L.ecah_vp_exchange_bytes.restype = c_size_t
+        L.ecah_vp_exchange_bytes.argtypes = [c_int32, c_int32, c_int32]
+        L.ecah_vp_step.restype = c_int32
+        L.ecah_vp_step.argtypes = [ctypes.POINTER(VPArgs), ctypes.POINTER(VPPeers), c_void_p]
+        L.ecah_vp_ipc_alloc.restype = c_int32
+        L.ecah_vp_ipc_alloc.argtypes = [c_size_t, ctypes.POINTER(c_void_p), c_void_p]
+        L.ecah_vp_ipc_open.restype = c_int32
+        L.ecah_vp_ipc_open.argtypes = [c_void_p, ctypes.POINTER(c_void_p)]
+        L.ecah_vp_ipc_close.restype = c_int32
+        L.ecah_vp_ipc_close.argtypes = [c_void_p]
+        L.ecah_vp_ipc_free.restype = c_int32
+        L.ecah_vp_ipc_free.argtypes = [c_void_p]
         if L.ecah_sampler_abi_version() != ABI_VERSION:
             raise EcahError("libecah_sampler.so ABI version mismatch")
         _lib = L

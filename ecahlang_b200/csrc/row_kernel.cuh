@@ -949,17 +949,43 @@ __device__ uint32_t radix_kth(const KParams& P, RSmem& S, int row, int R, unsign
 }
 
 // ------------------------------------------------ vocabulary-parallel local step
+// Where row `row`'s list and count go: this rank's own buffers, or, in the
+// fused step (FUSED), this rank's slot of exchange buffer h (every rank h,
+// epoch parity `par`).
+template <bool FUSED>
+__device__ __forceinline__ unsigned long long* vp_list(const KParams& P, int row, int h, unsigned par) {
+  if constexpr (!FUSED) return P.vp_cand + static_cast<long long>(row) * P.cand_cap;
+  return reinterpret_cast<unsigned long long*>(static_cast<char*>(P.vp_base[h]) + P.vp_lcand) +
+         ((static_cast<long long>(par) * P.vp_world + P.vp_rank) * P.vp_maxb + row) * P.cand_cap;
+}
+template <bool FUSED>
+__device__ __forceinline__ int* vp_count_slot(const KParams& P, int row, int h, unsigned par) {
+  if constexpr (!FUSED) return P.vp_count + row;
+  return reinterpret_cast<int*>(static_cast<char*>(P.vp_base[h]) + P.vp_lcount) +
+         (static_cast<long long>(par) * P.vp_world + P.vp_rank) * P.vp_maxb + row;
+}
+template <bool FUSED>
+__device__ __forceinline__ void vp_put(const KParams& P, int row, unsigned par, int o, unsigned long long v) {
+  if (o >= P.cand_cap) return;
+  const int nd = FUSED ? P.vp_world : 1;
+  for (int h = 0; h < nd; ++h) vp_list<FUSED>(P, row, h, par)[o] = v;
+}
+template <bool FUSED>
+__device__ __forceinline__ void vp_put_count(const KParams& P, int row, unsigned par, int c) {
+  const int nd = FUSED ? P.vp_world : 1;
+  for (int h = 0; h < nd; ++h) *vp_count_slot<FUSED>(P, row, h, par) = c;
+}
+
 // After the stream of a slice (P.V entries, first global id P.vocab_offset):
 // the slice's k-th largest key kth -- exact, from the per-key counts of the
 // candidates, which hold every entry with key >= F, or by radix select when
 // kth lies below F -- and every entry with key >= kth (ties included) in
 // vocab order as (key << 32 | global id): the first cand_cap of them, and
 // their count.
-template <int DT>
+template <int DT, bool FUSED>
 __device__ void vp_emit(const KParams& P, RSmem& S, int row, int R, int k, uint32_t kmax, uint32_t F, int fill,
-                        bool cand, int& ph) {
+                        bool cand, int& ph, unsigned par) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  unsigned long long* dst = P.vp_cand + static_cast<long long>(row) * P.cand_cap;
   const unsigned gofs = static_cast<unsigned>(P.vocab_offset);
   if (cand) {
     unsigned* cnth = reinterpret_cast<unsigned*>(&S.stage[0][0]) + kCntOff;   // zeroed before the gather
@@ -984,10 +1010,10 @@ __device__ void vp_emit(const KParams& P, RSmem& S, int row, int R, int k, uint3
       int o = rscan_i(__popc(m8), S, ph, &total);
       for (; m8; m8 &= m8 - 1u) {
         const int i = b0 + __ffs(m8) - 1;
-        if (o < P.cand_cap) dst[o] = (static_cast<unsigned long long>(gkey(S)[i]) << 32) | (gofs + gidx(S)[i]);
+        vp_put<FUSED>(P, row, par, o, (static_cast<unsigned long long>(gkey(S)[i]) << 32) | (gofs + gidx(S)[i]));
         ++o;
       }
-      if (tid == 0) P.vp_count[row] = total;
+      if (tid == 0) vp_put_count<FUSED>(P, row, par, total);
       return;
     }
   }
@@ -1022,25 +1048,38 @@ __device__ void vp_emit(const KParams& P, RSmem& S, int row, int R, int k, uint3
 #pragma unroll
     for (int j = 0; j < kEPT; ++j) {
       if ((m >> j) & 1u) {
-        if (o < P.cand_cap) dst[o] = (static_cast<unsigned long long>(ECAH_RKEY(w, j)) << 32) | (e0 + j);
+        vp_put<FUSED>(P, row, par, o, (static_cast<unsigned long long>(ECAH_RKEY(w, j)) << 32) | (e0 + j));
         ++o;
       }
     }
   });
-  if (tid == 0) P.vp_count[row] = total;
+  if (tid == 0) vp_put_count<FUSED>(P, row, par, total);
 }
 
+// The fused step's exchange and merge of one row, after its list is out:
+// flags every rank, waits (bounded) for every rank's list of the row, then
+// merges them and draws.  Defined with the merge (vp_kernel.cuh).
+template <int DT>
+__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch);
+
 // ------------------------------------------------------------ the kernel
-// One body for the sampler (VPL false) and for the vocabulary-parallel local
-// step (VPL: candidates only, then vp_emit).
-template <int DT, bool SPLIT, bool VPL>
+// One body for the sampler (VPM 0), the vocabulary-parallel local step (VPM
+// 1: candidates only, then vp_emit) and the fused vocabulary-parallel step
+// (VPM 2: vp_emit into every rank's exchange buffer, then vp_fused_finish).
+template <int DT, bool SPLIT, int VPM>
 __device__ __forceinline__ void row_body(const KParams& P) {
+  constexpr bool VPL = VPM != 0, FUSED = VPM == 2;
   using C = Codec<DT, 16>;
   extern __shared__ __align__(16) unsigned char dsm[];
   RSmem& S = *reinterpret_cast<RSmem*>(dsm);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = (P.V + kRound - 1) / kRound;
   const int PP = SPLIT ? P.parts : 1;   // CTAs per row: each streams a run of rounds
+  // fused step: this step's epoch (every row reads it before the last row
+  // to finish advances it) and its exchange parity
+  unsigned epoch = 0u;
+  if constexpr (FUSED) epoch = *static_cast<volatile unsigned*>(P.vp_base[P.vp_rank]) + 1u;
+  const unsigned par = epoch & 1u;
 
   for (int unit = blockIdx.x; unit < P.B * PP; unit += gridDim.x) {
     const int row = unit / PP, part = unit - row * PP;
@@ -1063,7 +1102,9 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       const long long kr = !sampled ? 1 : ((kk <= 0 || kk >= P.vocab_total) ? P.vocab_total : kk);
       N = static_cast<int>(min(kr, static_cast<long long>(P.V)));
       if (N > P.cand_cap) {
-        if (tid == 0) P.vp_count[row] = N;
+        if (tid == 0) vp_put_count<FUSED>(P, row, par, N);
+        if constexpr (FUSED) vp_fused_finish<DT>(P, S, row, epoch);
+        __syncthreads();
         continue;
       }
     }
@@ -1224,7 +1265,8 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     unsigned kmax, fmax;
     rmax2_u(best, N > 0 ? f : 0u, S, ph, &kmax, &fmax);
     if constexpr (VPL) {
-      vp_emit<DT>(P, S, row, R, N, kmax, fmax, fill, cand, ph);
+      vp_emit<DT, FUSED>(P, S, row, R, N, kmax, fmax, fill, cand, ph, par);
+      if constexpr (FUSED) vp_fused_finish<DT>(P, S, row, epoch);
       __syncthreads();  // shared state is reused by the next row
       continue;
     }
@@ -1588,14 +1630,14 @@ __device__ __forceinline__ void row_body(const KParams& P) {
 
 template <int DT, bool SPLIT>
 __global__ void __launch_bounds__(kT, 1) row_sample_kernel(const __grid_constant__ KParams P) {
-  row_body<DT, SPLIT, false>(P);
+  row_body<DT, SPLIT, 0>(P);
 }
 
 // Vocabulary-parallel local step: per row of the slice, the entries at or
 // above the slice's k-th largest key (vp_emit).  P.V is the slice length.
 template <int DT>
 __global__ void __launch_bounds__(kT, 1) vp_local_row_kernel(const __grid_constant__ KParams P) {
-  row_body<DT, false, true>(P);
+  row_body<DT, false, 1>(P);
 }
 
 #undef ECAH_RKEY

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 
 #include "row_kernel.cuh"
 #include "vp_kernel.cuh"
@@ -331,13 +332,8 @@ static int vp_check(const ecah_vp_args* a) {
   return ECAH_OK;
 }
 
-int ecah_vp_local(const ecah_vp_args* a, void* stream) {
-  const int st = vp_check(a);
-  if (st != ECAH_OK) return st;
-  if (a->batch == 0) return ECAH_OK;
-  if (!a->logits || !a->cand || !a->cand_count) return ECAH_ERR_NULL;
-  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
-  // the row kernel's stream and candidates over the slice (P.V = its length)
+// the row kernel's stream and candidates over a slice (P.V = its length)
+static KParams vp_kparams(const ecah_vp_args* a) {
   KParams P = {};
   P.logits = a->logits;
   P.row_stride = a->row_stride;
@@ -358,6 +354,16 @@ int ecah_vp_local(const ecah_vp_args* a, void* stream) {
   P.vocab_offset = a->vocab_offset;
   P.vocab_total = a->vocab;
   P.cand_cap = a->cand_cap;
+  return P;
+}
+
+int ecah_vp_local(const ecah_vp_args* a, void* stream) {
+  const int st = vp_check(a);
+  if (st != ECAH_OK) return st;
+  if (a->batch == 0) return ECAH_OK;
+  if (!a->logits || !a->cand || !a->cand_count) return ECAH_ERR_NULL;
+  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
+  KParams P = vp_kparams(a);
   P.vp_cand = reinterpret_cast<unsigned long long*>(a->cand);
   P.vp_count = a->cand_count;
   const int smem = static_cast<int>(sizeof(rk::RSmem));
@@ -370,6 +376,90 @@ int ecah_vp_local(const ecah_vp_args* a, void* stream) {
   return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
 
+// Exchange-buffer layout of the fused step (the same on every rank).
+struct VpXLayout {
+  long long flag, count, cand, total;
+};
+static VpXLayout vp_xlayout(long long maxb, long long world, long long cap) {
+  auto al = [](long long x) { return (x + 255) & ~255LL; };
+  VpXLayout L;
+  long long off = 256;   // header: epoch, finished-row counter, error word
+  L.flag = off; off += al(4 * world * maxb);
+  L.count = off; off += al(4 * 2 * world * maxb);
+  L.cand = off; off += al(8 * 2 * world * maxb * cap);
+  L.total = off;
+  return L;
+}
+
+size_t ecah_vp_exchange_bytes(int32_t max_batch, int32_t world, int32_t cand_cap) {
+  if (max_batch < 1 || world < 1 || world > 64 || cand_cap < 1) return 0;
+  return static_cast<size_t>(vp_xlayout(max_batch, world, cand_cap).total);
+}
+
+int ecah_vp_step(const ecah_vp_args* a, const ecah_vp_peers* x, void* stream) {
+  const int st = vp_check(a);
+  if (st != ECAH_OK) return st;
+  if (!x) return ECAH_ERR_NULL;
+  if (x->rank < 0 || x->rank >= a->world || x->max_batch < a->batch) return ECAH_ERR_SHAPE;
+  if (a->batch == 0) return ECAH_OK;
+  if (!a->logits || !a->out || !x->base) return ECAH_ERR_NULL;
+  if (!a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
+  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
+  KParams P = vp_kparams(a);
+  const VpXLayout L = vp_xlayout(x->max_batch, a->world, a->cand_cap);
+  P.vp_base = x->base;
+  P.vp_world = a->world;
+  P.vp_rank = x->rank;
+  P.vp_maxb = x->max_batch;
+  P.vp_lflag = L.flag;
+  P.vp_lcount = L.count;
+  P.vp_lcand = L.cand;
+  P.vp_timeout_ns = static_cast<unsigned long long>(x->timeout_us) * 1000ull;
+  P.uniforms = a->uniforms;
+  P.philox_state = reinterpret_cast<unsigned long long*>(a->philox_state);
+  P.out = a->out;
+  P.row_stats = a->row_stats;
+  const int smem = static_cast<int>(sizeof(rk::RSmem));
+  const int sms = device_sms();
+  if (sms <= 0) return ECAH_ERR_LAUNCH;
+  const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
+  KernelFn fn = a->dtype == ECAH_DTYPE_F16 ? rk::vp_step_row_kernel<ECAH_DTYPE_F16> : rk::vp_step_row_kernel<ECAH_DTYPE_BF16>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
+  fn<<<grid, rk::kT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
+int ecah_vp_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return ECAH_ERR_NULL;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return ECAH_ERR_LAUNCH;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return ECAH_ERR_LAUNCH;
+  }
+  return ECAH_OK;
+}
+
+int ecah_vp_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return ECAH_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
+int ecah_vp_ipc_close(void* ptr) {
+  if (!ptr) return ECAH_ERR_NULL;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
+int ecah_vp_ipc_free(void* ptr) {
+  if (!ptr) return ECAH_ERR_NULL;
+  return cudaFree(ptr) == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
 int ecah_vp_merge(const ecah_vp_args* a, void* stream) {
   const int st = vp_check(a);
   if (st != ECAH_OK) return st;
@@ -378,7 +468,7 @@ int ecah_vp_merge(const ecah_vp_args* a, void* stream) {
   if (!a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
   if (!a->workspace || a->workspace_bytes < kMinWorkspace) return ECAH_ERR_WORKSPACE;
   vp::VParams P = {};
-  P.B = a->batch; P.V = a->vocab;
+  P.B = a->batch; P.V = a->vocab; P.Bs = a->batch;
   P.temperature = a->temperature; P.top_k = a->top_k; P.top_p = a->top_p;
   P.cap = a->cand_cap; P.world = a->world;
   P.all_cand = reinterpret_cast<const unsigned long long*>(a->all_cand);

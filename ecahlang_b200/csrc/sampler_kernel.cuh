@@ -90,6 +90,12 @@ struct KParams {
   int cand_cap;                     // list entries per row
   unsigned long long* vp_cand;      // [B, cand_cap] key << 32 | global id, vocab order
   int* vp_count;                    // [B] entries at or above the k-th largest key
+  // fused vocabulary-parallel step (lists written straight into every rank's
+  // exchange buffer, then a per-row flag; see vp_kernel.cuh)
+  void* const* vp_base;             // [vp_world] every rank's exchange buffer, mapped here
+  int vp_world, vp_rank, vp_maxb;   // ranks, this rank, rows the buffers hold
+  long long vp_lflag, vp_lcount, vp_lcand;   // region offsets in an exchange buffer
+  unsigned long long vp_timeout_ns; // per wait on another rank's flag
 };
 
 constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private

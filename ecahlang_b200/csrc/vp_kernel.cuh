@@ -16,9 +16,29 @@
 // inverse-CDF draw in global vocab order with the row's uniform, so every
 // rank returns the same token.  Op order, masses and tie rules are those of
 // the other sampler kernels.
+//
+// The fused step (rk::vp_step_row_kernel) does all of it in one kernel over
+// NVLink peer memory.  Every rank owns an exchange buffer that every other
+// rank has mapped (CUDA IPC):
+//   [0, 256)  header: step epoch (u32 at 0), finished-row counter (u32 at 4),
+//             error word (i32 at 8: a wait ran out);
+//   flag      [world][maxb] u32: rank g sets flag[g][row] = epoch once its
+//             list of the row is in this buffer;
+//   count     [2][world][maxb] i32 and cand [2][world][maxb][cap] u64: rank
+//             g's counts and lists, double-buffered by epoch parity.
+// Per row a CTA streams its slice, stores the list and count into its slot of
+// every rank's buffer (plain stores over NVLink, no multicast), fences at
+// system scope, sets the row's flag in every buffer (st.release.sys), waits
+// for every rank's flag in its own buffer (ld.acquire.sys, bounded by
+// vp_timeout_ns), and merges the row from its own buffer.  Ranks take rows
+// in the same order, and a row waits only on the same row of other ranks.
+// A rank reaches step s + 2 only after every rank has flagged every row of
+// step s + 1, which each rank does after finishing step s, so the parity
+// buffer a rank reads is never rewritten under it; flags only grow, so a
+// flag read late compares >= the epoch.
 #pragma once
 
-#include "stream_kernel.cuh"
+#include "row_kernel.cuh"
 
 namespace ecah {
 namespace vp {
@@ -31,77 +51,83 @@ constexpr int kWin = 4096;               // merge histogram: keys below the row 
 // what the merge reads (the local step runs on the row kernel's KParams)
 struct VParams {
   int B, V;
+  int Bs;                                 // rows between two ranks' lists (B, or the buffers' maxb)
   const float* temperature;
   const int* top_k;
   const float* top_p;
   int cap;                                // candidates per row and rank
   int world;
-  const unsigned long long* all_cand;     // [world, B, cap]
-  const int* all_count;                   // [world, B] (> cap: truncated)
+  const unsigned long long* all_cand;     // [world, Bs, cap]
+  const int* all_count;                   // [world, Bs] (> cap: truncated)
   const float* uniforms;
   unsigned long long* philox_state;
   unsigned* done_counter;
+  unsigned* epoch;                        // fused step: advanced with the Philox offset
   int* out;
   float* row_stats;
 };
 
 // ------------------------------------------------------------ merge step
+template <int NT>
 struct MSmem {
   unsigned long long c[kMaxMerged];   // merged entries, rank order (= vocab order)
   unsigned cnt[kWin];                 // counts per key, bin b = key kmax - b
-  float red[kMW];
-  unsigned ured[kMW];
+  float red[NT / 32];
+  unsigned ured[NT / 32];
   int ofs[65];
   int ib[8];
   float fb[8];
 };
 
+template <int NT>
 __device__ __forceinline__ unsigned mblock_max(unsigned v, unsigned* red) {
   v = __reduce_max_sync(0xFFFFFFFFu, v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   unsigned m = 0u;
-  for (int w = 0; w < kMW; ++w) m = max(m, red[w]);
+  for (int w = 0; w < NT / 32; ++w) m = max(m, red[w]);
   __syncthreads();
   return m;
 }
 
+template <int NT>
 __device__ __forceinline__ unsigned mblock_min(unsigned v, unsigned* red) {
   v = __reduce_min_sync(0xFFFFFFFFu, v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   unsigned m = 0xFFFFFFFFu;
-  for (int w = 0; w < kMW; ++w) m = min(m, red[w]);
+  for (int w = 0; w < NT / 32; ++w) m = min(m, red[w]);
   __syncthreads();
   return m;
 }
 
-template <int DT>
-__global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ VParams P) {
+// One row of the merge by a CTA of NT threads.  `lost`: a rank's list never
+// arrived (the fused step's wait ran out); the row gets -1.
+template <int DT, int NT>
+__device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int row, bool lost) {
+  constexpr int NW = NT / 32;
   using C = Codec<DT, 16>;
-  __shared__ MSmem S;
-  const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
 
   // merged entries of the row: rank by rank (each rank's list is in vocab order)
   if (tid == 0) {
     int acc = 0, bad = 0;
     for (int g = 0; g < P.world; ++g) {
-      const int c = P.all_count[static_cast<long long>(g) * P.B + row];
+      const int c = lost ? 0 : P.all_count[static_cast<long long>(g) * P.Bs + row];
       if (c > P.cap) bad = 1;
       S.ofs[g] = acc;
       acc += min(c, P.cap);
     }
     S.ofs[P.world] = acc;
-    S.ib[0] = bad;
+    S.ib[0] = bad | (lost ? 1 : 0);
   }
   __syncthreads();
   const int total = S.ofs[P.world];
   const bool truncated = S.ib[0] != 0;
   for (int g = 0; g < P.world; ++g) {
     const int c = S.ofs[g + 1] - S.ofs[g];
-    const unsigned long long* src = P.all_cand + (static_cast<long long>(g) * P.B + row) * P.cap;
-    for (int i = tid; i < c; i += kMT) S.c[S.ofs[g] + i] = src[i];
+    const unsigned long long* src = P.all_cand + (static_cast<long long>(g) * P.Bs + row) * P.cap;
+    for (int i = tid; i < c; i += NT) S.c[S.ofs[g] + i] = src[i];
   }
   __syncthreads();
 
@@ -114,12 +140,12 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
 
   // row max and its lowest id
   unsigned km = 0u;
-  for (int i = tid; i < total; i += kMT) km = max(km, static_cast<unsigned>(S.c[i] >> 32));
-  const unsigned kmax = mblock_max(km, S.ured);
+  for (int i = tid; i < total; i += NT) km = max(km, static_cast<unsigned>(S.c[i] >> 32));
+  const unsigned kmax = mblock_max<NT>(km, S.ured);
   unsigned fid = 0xFFFFFFFFu;
-  for (int i = tid; i < total; i += kMT)
+  for (int i = tid; i < total; i += NT)
     if (static_cast<unsigned>(S.c[i] >> 32) == kmax) fid = min(fid, static_cast<unsigned>(S.c[i] & 0xFFFFFFFFu));
-  const unsigned first = mblock_min(fid, S.ured);
+  const unsigned first = mblock_min<NT>(fid, S.ured);
   const float ymax = C::value(kmax);
   const float M = __fdiv_rn(ymax, T);
   // a truncated sampled row is refused whatever its lists hold (a rank whose
@@ -146,11 +172,11 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
       for (int i = 0; i < c; ++i) lo = min(lo, static_cast<unsigned>(S.c[S.ofs[tid] + i] >> 32));
       fl = (c > 0) ? lo : 0u;
     }
-    uint32_t F = mblock_max(fl, S.ured);
+    uint32_t F = mblock_max<NT>(fl, S.ured);
     if (kmax >= static_cast<uint32_t>(kWin) && F < kmax - static_cast<uint32_t>(kWin - 1)) F = kmax - static_cast<uint32_t>(kWin - 1);
-    for (int b = tid; b < kWin; b += kMT) S.cnt[b] = 0u;
+    for (int b = tid; b < kWin; b += NT) S.cnt[b] = 0u;
     __syncthreads();
-    for (int i = tid; i < total; i += kMT) {
+    for (int i = tid; i < total; i += NT) {
       const unsigned key = static_cast<unsigned>(S.c[i] >> 32);
       if (key >= F) atomicAdd(&S.cnt[kmax - key], 1u);
     }
@@ -183,7 +209,7 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
     if (ok && topp) {
       const int bk = static_cast<int>(kmax - key_lo_k);
       float* mb = reinterpret_cast<float*>(S.cnt);
-      for (int b = tid; b < kWin; b += kMT) {
+      for (int b = tid; b < kWin; b += NT) {
         const unsigned cn = S.cnt[b];
         mb[b] = (b <= bk && cn) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
       }
@@ -203,7 +229,7 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
     if (ok) {
       // inverse CDF over the merged entries in vocab order (thread t: a contiguous stretch)
       const uint32_t kdraw = max(key_lo, key_cut);
-      const int per = (total + kMT - 1) / kMT;
+      const int per = (total + NT - 1) / NT;
       const int i0 = min(total, tid * per), i1 = min(total, i0 + per);
       float acc = 0.f;
       int lastp = -1;
@@ -224,7 +250,7 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
       if (lane == 31) S.red[tid >> 5] = incl;
       __syncthreads();
       float base = 0.f, tot = 0.f;
-      for (int w = 0; w < kMW; ++w) {
+      for (int w = 0; w < NW; ++w) {
         if (w < (tid >> 5)) base += S.red[w];
         tot += S.red[w];
       }
@@ -244,8 +270,8 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
         if (mine == INT_MAX) mine = lastp;
       }
       __syncthreads();
-      const unsigned pick = mblock_min(static_cast<unsigned>(mine), S.ured);
-      const unsigned last = mblock_max(static_cast<unsigned>(lastp + 1), S.ured);
+      const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured);
+      const unsigned last = mblock_max<NT>(static_cast<unsigned>(lastp + 1), S.ured);
       if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(S.c[pick] & 0xFFFFFFFFu);
       else if (last > 0u) result = static_cast<int>(S.c[last - 1u] & 0xFFFFFFFFu);
       else ok = false;
@@ -253,7 +279,7 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
   }
 
   if (tid == 0) {
-    P.out[row] = (greedy || ok) ? min(result, P.V - 1) : -1;
+    P.out[row] = (!lost && (greedy || ok)) ? min(result, P.V - 1) : -1;
     if (P.row_stats) {
       float* st = P.row_stats + 4ll * row;
       if (greedy) { st[0] = ymax; st[1] = ymax; st[2] = ymax; st[3] = 1.0f; }
@@ -264,12 +290,14 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
         st[3] = Z;
       }
     }
-    if (!P.uniforms && P.philox_state) {
-      // the last row to finish advances the Philox offset
+    const bool philox = !P.uniforms && P.philox_state;
+    if (philox || P.epoch) {
+      // the last row to finish advances the Philox offset and the epoch
       __threadfence();
       const unsigned prev = atomicAdd(P.done_counter, 1u);
       if (prev == static_cast<unsigned>(P.B) - 1u) {
-        P.philox_state[1] += 1ull;
+        if (philox) P.philox_state[1] += 1ull;
+        if (P.epoch) *P.epoch += 1u;
         *P.done_counter = 0u;
         __threadfence();
       }
@@ -277,5 +305,86 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
   }
 }
 
+template <int DT>
+__global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ VParams P) {
+  __shared__ MSmem<kMT> S;
+  merge_row<DT, kMT>(P, S, blockIdx.x, false);
+}
+
 }  // namespace vp
+
+// ------------------------------------------------------------ fused step
+namespace rk {
+
+constexpr unsigned kSpinMax = 1u << 24;   // backstop to the time limit of a wait
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+template <int DT>
+__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch) {
+  const int tid = threadIdx.x;
+  const int world = P.vp_world;
+  char* own = static_cast<char*>(P.vp_base[P.vp_rank]);
+  int* err = reinterpret_cast<int*>(own + 8);
+  // the row's list and count went to every rank's buffer: make them visible
+  // system-wide before any flag says so
+  __threadfence_system();
+  __syncthreads();
+  if (tid < world)
+    st_release_sys(reinterpret_cast<unsigned*>(static_cast<char*>(P.vp_base[tid]) + P.vp_lflag) +
+                       static_cast<long long>(P.vp_rank) * P.vp_maxb + row, epoch);
+  int lost = 0;
+  if (tid < world) {
+    const unsigned* fl = reinterpret_cast<const unsigned*>(own + P.vp_lflag) + static_cast<long long>(tid) * P.vp_maxb + row;
+    if (*static_cast<volatile int*>(err) != 0) {
+      lost = 1;   // an earlier wait of this step ran out: wait no more
+    } else {
+      const unsigned long long t0 = global_ns();
+      for (unsigned it = 0;; ++it) {
+        if (static_cast<int>(ld_acquire_sys(fl) - epoch) >= 0) break;
+        if (it >= kSpinMax || global_ns() - t0 > P.vp_timeout_ns) {
+          lost = 1;
+          atomicExch(err, 1);
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  lost = __syncthreads_or(lost);
+  vp::VParams M;
+  M.B = P.B; M.V = P.vocab_total; M.Bs = P.vp_maxb;
+  M.temperature = P.temperature; M.top_k = P.top_k; M.top_p = P.top_p;
+  M.cap = P.cand_cap; M.world = world;
+  const long long slot0 = static_cast<long long>(epoch & 1u) * world * P.vp_maxb;
+  M.all_cand = reinterpret_cast<const unsigned long long*>(own + P.vp_lcand) + slot0 * P.cand_cap;
+  M.all_count = reinterpret_cast<const int*>(own + P.vp_lcount) + slot0;
+  M.uniforms = P.uniforms; M.philox_state = P.philox_state;
+  M.done_counter = reinterpret_cast<unsigned*>(own + 4);
+  M.epoch = reinterpret_cast<unsigned*>(own);
+  M.out = P.out; M.row_stats = P.row_stats;
+  // the stages are free once every thread has stored its part of the list
+  vp::merge_row<DT, kT>(M, *reinterpret_cast<vp::MSmem<kT>*>(&S.stage[0][0]), row, lost != 0);
+}
+
+// The whole vocabulary-parallel step for this rank: stream, local list into
+// every rank's exchange buffer, flags, waits, merge and draw.
+template <int DT>
+__global__ void __launch_bounds__(kT, 1) vp_step_row_kernel(const __grid_constant__ KParams P) {
+  row_body<DT, false, 2>(P);
+}
+
+}  // namespace rk
 }  // namespace ecah

@@ -11,6 +11,12 @@ vocab order with global ids (``ecah_vp_local``); since the row's k-th largest
 key is at least every slice's, the union holds the row's whole top-k set, and
 ``ecah_vp_merge`` finishes the row exactly as the single-GPU sampler does.
 Rows need 1 <= top_k <= cand_cap (or T <= 0); other rows come back as -1.
+
+Two exchanges: ``exchange="peer"`` runs the whole step as one kernel per rank
+(``ecah_vp_step``) that stores each row's list straight into every rank's
+exchange buffer over NVLink (CUDA IPC mappings, see ``PeerExchange``);
+otherwise a callable all-gathers the lists between ``ecah_vp_local`` and
+``ecah_vp_merge`` (``nccl_exchange``: NCCL over NVLink).
 """
 from __future__ import annotations
 
@@ -20,7 +26,7 @@ from typing import Callable, Optional
 import torch
 
 from . import _abi
-from ._abi import VPArgs, check, lib
+from ._abi import VPArgs, VPPeers, check, lib
 from .sampler import PenaltyState, new_philox_state, resolve_device
 
 _DTYPES = {torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16}
@@ -47,13 +53,94 @@ def nccl_exchange(group=None) -> Callable[[torch.Tensor, torch.Tensor, torch.Ten
     return run
 
 
+class _DeviceWords:
+    """__cuda_array_interface__ of n int32 words at a raw device address."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Exchange buffers of the fused step: this rank's buffer
+    (``ecah_vp_ipc_alloc``: zero-filled, with a CUDA IPC handle) and every
+    other rank's, mapped into this process (``ecah_vp_ipc_open``).
+
+    ``all_gather(obj)`` returns every rank's object in rank order and
+    ``barrier()`` waits for every rank; both default to torch.distributed on
+    ``group`` (any backend: only the 64-byte handles travel).  The buffers stay
+    mapped until ``close``, which every rank calls once its last step is done.
+    """
+
+    def __init__(self, max_batch: int, world: int, rank: int, cand_cap: int, device,
+                 timeout_us: int = 1_000_000, group=None,
+                 all_gather: Optional[Callable] = None, barrier: Optional[Callable] = None):
+        if all_gather is None or barrier is None:
+            import torch.distributed as dist
+
+            def _all_gather(obj):
+                out = [None] * world
+                dist.all_gather_object(out, obj, group=group)
+                return out
+            all_gather = all_gather or _all_gather
+            barrier = barrier or (lambda: dist.barrier(group=group))
+        L = lib()
+        self.device = resolve_device(device)
+        self.world, self.rank, self.max_batch = world, rank, max_batch
+        self.nbytes = L.ecah_vp_exchange_bytes(max_batch, world, cand_cap)
+        if self.nbytes == 0:
+            raise ValueError("vocab-parallel exchange: bad max_batch / world / cand_cap")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _abi.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            check(L.ecah_vp_ipc_alloc(self.nbytes, ctypes.byref(own), handle), "ecah_vp_ipc_alloc")
+        self.own = own.value
+        self._mapped = []
+        self._barrier = barrier
+        handles = all_gather(bytes(handle))
+        bases = []
+        with torch.cuda.device(self.device):
+            for g, h in enumerate(handles):
+                if g == rank:
+                    bases.append(self.own)
+                    continue
+                p = ctypes.c_void_p()
+                check(L.ecah_vp_ipc_open((ctypes.c_ubyte * _abi.IPC_HANDLE_BYTES).from_buffer_copy(h),
+                                         ctypes.byref(p)), "ecah_vp_ipc_open")
+                self._mapped.append(p.value)
+                bases.append(p.value)
+        self.base = torch.tensor(bases, dtype=torch.int64, device=self.device)
+        # header words: [0] step epoch, [1] finished rows, [2] error (a wait ran out)
+        self.header = torch.as_tensor(_DeviceWords(self.own, 64), device=self.device)
+        self.peers = VPPeers(rank, max_batch, self.base.data_ptr(), timeout_us)
+        barrier()   # every rank has mapped every buffer before any step stores into them
+
+    def error(self) -> int:
+        """Nonzero once a wait on another rank's row ran out (synchronises)."""
+        return int(self.header[2].item())
+
+    def close(self) -> None:
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._barrier()   # no rank stores into another's buffer any more
+        L = lib()
+        with torch.cuda.device(self.device):
+            for p in self._mapped:
+                check(L.ecah_vp_ipc_close(p), "ecah_vp_ipc_close")
+            self._mapped = []
+            self.header = None
+            check(L.ecah_vp_ipc_free(self.own), "ecah_vp_ipc_free")
+        self.own = None
+
+
 class VocabParallelSampler:
     """Per-rank state of the vocab-parallel sampler (buffers sized for
     max_batch, Philox state seeded identically on every rank)."""
 
     def __init__(self, max_batch: int, vocab: int, world: int, rank: int, dtype: torch.dtype,
                  device="cuda", seed: int = 0, cand_cap: int = 256,
-                 exchange: Optional[Callable] = None):
+                 exchange=None, timeout_us: int = 1_000_000):
         if dtype not in _DTYPES:
             raise RuntimeError(f"vocab-parallel sampling takes fp16/bf16 logits, not {dtype}")
         if world * cand_cap > 2048:
@@ -70,7 +157,12 @@ class VocabParallelSampler:
         self.workspace = torch.zeros(256, dtype=torch.uint8, device=dev)
         self.philox_state = new_philox_state(seed, 0, dev)
         self.out = torch.zeros(max_batch, dtype=torch.int32, device=dev)
-        self.exchange = exchange if exchange is not None else nccl_exchange()
+        self.peer = None
+        if exchange == "peer":
+            self.peer = PeerExchange(max_batch, world, rank, cand_cap, dev, timeout_us=timeout_us)
+            self.exchange = None
+        else:
+            self.exchange = exchange if exchange is not None else nccl_exchange()
 
     def _args(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats):
         B = logits.shape[0]
@@ -162,9 +254,16 @@ class VocabParallelSampler:
                  penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
                  rep_factor: Optional[torch.Tensor] = None, row_stats: Optional[torch.Tensor] = None) -> torch.Tensor:
         """logits: this rank's [B, vocab_local] slice.  Local candidates, the
-        exchange, then the merge; returns the [B] ids (identical on every rank)."""
+        exchange, then the merge (with ``exchange="peer"``: one fused kernel);
+        returns the [B] ids (identical on every rank)."""
         self._check(logits, temperature, top_k, top_p, uniforms)
         B = logits.shape[0]
+        if self.peer is not None:
+            a = self._args(logits, temperature.reshape(-1), top_k, top_p, uniforms, penalty, row_slot,
+                           rep_factor, row_stats)
+            check(lib().ecah_vp_step(ctypes.byref(a), ctypes.byref(self.peer.peers),
+                                     torch.cuda.current_stream(self.device).cuda_stream), "ecah_vp_step")
+            return self.out[:B]
         cand, count = self.local(logits, temperature, top_k, top_p, penalty, row_slot, rep_factor)
         if B == self.cand.shape[0]:
             all_cand, all_count = self.all_cand, self.all_count
@@ -173,3 +272,8 @@ class VocabParallelSampler:
             all_count = self.all_count.view(-1)[: self.world * B].view(self.world, B)
         self.exchange(cand, count, all_cand, all_count)
         return self.merge(all_cand, all_count, temperature, top_k, top_p, uniforms, row_stats)
+
+    def close(self) -> None:
+        """Unmaps the peer exchange buffers (every rank, after its last step)."""
+        if self.peer is not None:
+            self.peer.close()

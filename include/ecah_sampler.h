@@ -217,6 +217,38 @@ typedef struct ecah_vp_args {
 ECAH_API int ecah_vp_local(const ecah_vp_args* args, void* stream);
 ECAH_API int ecah_vp_merge(const ecah_vp_args* args, void* stream);
 
+/*
+ * The whole vocab-parallel step in one kernel per rank, with the exchange
+ * over NVLink peer memory instead of an all-gather.  Each rank owns an
+ * exchange buffer of ecah_vp_exchange_bytes(max_batch, world, cand_cap) bytes
+ * (ecah_vp_ipc_alloc: zero-filled, with a CUDA IPC handle) and maps every
+ * other rank's (ecah_vp_ipc_open).  Per row, the kernel stores its list and
+ * count into its slot of every rank's buffer, sets the row's flag there, waits
+ * for every rank's flag in its own buffer (at most timeout_us per wait), then
+ * merges and draws as ecah_vp_merge does.  Every rank launches every step with
+ * the same batch, parameters and uniforms (or Philox state).  A wait that runs
+ * out sets the error word (int32 at byte 8 of this rank's buffer); that row
+ * and the rest of the step get out = -1.  args->cand, cand_count, all_cand,
+ * all_count, workspace are not used.  The step counter lives in the buffer,
+ * so the launch can be captured in a CUDA graph.  Ranks on one GPU are not
+ * supported (their kernels would wait on each other).
+ */
+typedef struct ecah_vp_peers {
+  int32_t rank;               /* this rank, 0 .. world-1                          */
+  int32_t max_batch;          /* rows the exchange buffers were sized for         */
+  void* const* base;          /* device array [world]: every rank's exchange
+                                 buffer as mapped in this process (own at rank)  */
+  uint32_t timeout_us;        /* per wait on another rank's row                   */
+} ecah_vp_peers;
+
+ECAH_API size_t ecah_vp_exchange_bytes(int32_t max_batch, int32_t world, int32_t cand_cap);
+ECAH_API int ecah_vp_step(const ecah_vp_args* args, const ecah_vp_peers* peers, void* stream);
+/* CUDA IPC helpers for the exchange buffers (handle: 64 bytes). */
+ECAH_API int ecah_vp_ipc_alloc(size_t bytes, void** ptr, void* handle);
+ECAH_API int ecah_vp_ipc_open(const void* handle, void** ptr);
+ECAH_API int ecah_vp_ipc_close(void* ptr);
+ECAH_API int ecah_vp_ipc_free(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,20 @@ def test_vocab_parallel_rejects_bad_arguments_without_a_device(L):
     assert L.ecah_vp_local(vp(world=16, cand_cap=256), None) == 3   # world * cap > 2048
     assert L.ecah_vp_local(vp(), None) == 1                         # parameter arrays missing
     assert L.ecah_vp_merge(vp(batch=0), None) == 0
+    # parameter arrays present (never dereferenced: every call below returns before a launch)
+    par = dict(temperature=16, top_k=16, top_p=16)
+    peers = _abi.VPPeers(0, 4, None, 1000)
+    assert L.ecah_vp_step(vp(**par), None, None) == 1                 # no peers
+    assert L.ecah_vp_step(vp(**par), ctypes.byref(_abi.VPPeers(2, 4, None, 1000)), None) == 3  # rank >= world
+    assert L.ecah_vp_step(vp(**par), ctypes.byref(_abi.VPPeers(0, 3, None, 1000)), None) == 3  # max_batch < batch
+    assert L.ecah_vp_step(vp(**par), ctypes.byref(peers), None) == 1  # logits, out and buffers missing
+    assert L.ecah_vp_step(vp(batch=0), ctypes.byref(peers), None) == 0
+    assert L.ecah_vp_exchange_bytes(0, 2, 64) == 0
+    # header, flags [2][4] u32, counts [2][2][4] i32, lists [2][2][4][64] u64, each 256-aligned
+    assert L.ecah_vp_exchange_bytes(4, 2, 64) == 256 + 256 + 256 + 2 * 2 * 4 * 64 * 8
+    assert L.ecah_vp_ipc_open(None, None) == 1
+    assert L.ecah_vp_ipc_close(None) == 1
+    assert L.ecah_vp_ipc_free(None) == 1
 
 
 def test_product_path_fails_loudly_without_library(monkeypatch):

@@ -3,6 +3,7 @@ every rank's slice goes through ecah_vp_local, the lists are stacked in rank
 order as the all-gather would, and ecah_vp_merge runs once per rank; every
 rank must return the same ids, equal to the CPU oracle on the full rows.
 With two GPUs the same runs as two NCCL ranks."""
+import ctypes
 import os
 import socket
 
@@ -10,6 +11,7 @@ import numpy as np
 import pytest
 import torch
 
+from ecahlang_b200 import _abi
 from ecahlang_b200 import sampler as S
 from ecahlang_b200 import workloads as W
 from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
@@ -169,6 +171,136 @@ def _nccl_rank(rank, world, port, outdir):
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+class _Raw:
+    """__cuda_array_interface__ over n words of a raw device address."""
+
+    def __init__(self, ptr, n, typestr):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _al(x):
+    return (x + 255) & ~255
+
+
+def test_vp_step_wait_runs_out_and_reports():
+    """The fused step on one GPU with world = 2 and no second rank: the
+    stand-in for rank 1's buffer is never flagged, so every wait runs out
+    after timeout_us.  The step returns -1 for every row, sets the error word
+    and still advances the epoch; the rows' lists and counts sit in rank 0's
+    slot of both buffers, as ecah_vp_local writes them, with the rows' flags
+    at epoch 1.  A second step finds the error word set and waits no more."""
+    dev = torch.device("cuda")
+    B, V, world, cap = 8, 4000, 2, 64
+    x, T, K, P, U = vp_case(31, B, V)
+    T[:] = 1.0
+    K[:] = [1, 5, 20, 64, 65, 0, 3, 10]          # rows 4 and 5: k > cap, count only
+    off, loc = split_vocab(V, world, 0)
+    xd = torch.from_numpy(x[:, off:off + loc]).to(torch.bfloat16).to(dev).contiguous()
+    Td, Kd, Pd, Ud = (torch.from_numpy(a).to(dev) for a in (T, K, P, U))
+    smp = VocabParallelSampler(B, V, world, 0, torch.bfloat16, dev, seed=5, cand_cap=cap,
+                               exchange=lambda *a: None)
+    c_ref, n_ref = (t.clone() for t in smp.local(xd, Td, Kd, Pd))
+    L = _abi.lib()
+    nbytes = L.ecah_vp_exchange_bytes(B, world, cap)
+    bufs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        _abi.check(L.ecah_vp_ipc_alloc(nbytes, ctypes.byref(p), (ctypes.c_ubyte * 64)()), "alloc")
+        bufs.append(p.value)
+    try:
+        base = torch.tensor(bufs, dtype=torch.int64, device=dev)
+        peers = _abi.VPPeers(0, B, base.data_ptr(), 20000)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        a = smp._args(xd, Td, Kd, Pd, Ud, None, None, None, None)
+        _abi.check(L.ecah_vp_step(ctypes.byref(a), ctypes.byref(peers), stream), "ecah_vp_step")
+        torch.cuda.synchronize()
+        assert (smp.out[:B].cpu() == -1).all()
+        hdr = torch.as_tensor(_Raw(bufs[0], 64, "<i4"), device=dev).cpu()
+        assert hdr[0] == 1 and hdr[1] == 0 and hdr[2] == 1       # epoch, finished rows, error
+        lflag = 256
+        lcount = lflag + _al(4 * world * B)
+        lcand = lcount + _al(4 * 2 * world * B)
+        for buf in bufs:
+            flags = torch.as_tensor(_Raw(buf + lflag, world * B, "<i4"), device=dev).cpu().view(world, B)
+            assert (flags[0] == 1).all() and (flags[1] == 0).all()
+            cnt = torch.as_tensor(_Raw(buf + lcount, 2 * world * B, "<i4"), device=dev).cpu().view(2, world, B)
+            lists = torch.as_tensor(_Raw(buf + lcand, 2 * world * B * cap, "<i8"), device=dev).cpu()
+            lists = lists.view(2, world, B, cap)
+            assert torch.equal(cnt[1, 0], n_ref.cpu())                # epoch 1: parity 1, rank 0's slot
+            for r in range(B):
+                m = min(int(n_ref[r]), cap) if n_ref[r] <= cap else 0
+                assert torch.equal(lists[1, 0, r, :m], c_ref[r, :m].cpu()), r
+        _abi.check(L.ecah_vp_step(ctypes.byref(a), ctypes.byref(peers), stream), "ecah_vp_step")
+        torch.cuda.synchronize()
+        assert (smp.out[:B].cpu() == -1).all()
+        hdr = torch.as_tensor(_Raw(bufs[0], 64, "<i4"), device=dev).cpu()
+        assert hdr[0] == 2 and hdr[2] == 1
+    finally:
+        torch.cuda.synchronize()
+        for p in bufs:
+            _abi.check(L.ecah_vp_ipc_free(p), "free")
+
+
+def _peer_rank(rank, world, port, outdir):
+    """One rank of the fused step over NVLink peer memory; gloo carries only
+    the IPC handles."""
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        dev = torch.device("cuda", rank)
+        B, V = 48, 20011
+        x, T, K, P, U = vp_case(41, B, V)
+        off, loc = split_vocab(V, world, rank)
+        xd = torch.from_numpy(x[:, off:off + loc]).to(torch.bfloat16).to(dev).contiguous()
+        Td, Kd, Pd, Ud = (torch.from_numpy(a).to(dev) for a in (T, K, P, U))
+        smp = VocabParallelSampler(B, V, world, rank, torch.bfloat16, dev, seed=9, cand_cap=2048 // world,
+                                   exchange="peer", timeout_us=5_000_000)
+        res = {}
+        for step, b in enumerate((B, 20, B)):     # both parities, a smaller batch
+            res[f"s{step}"] = smp(xd[:b], Td[:b], Kd[:b], Pd[:b], uniforms=Ud[:b]).cpu().numpy().copy()
+        res["philox"] = smp(xd, Td, Kd, Pd).cpu().numpy().copy()
+        # two steps captured in a CUDA graph, replayed twice (the epoch lives on the device)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            smp(xd, Td, Kd, Pd, uniforms=Ud)
+            smp(xd, Td, Kd, Pd, uniforms=Ud)
+        for i in range(2):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            res[f"graph{i}"] = smp.out[:B].cpu().numpy().copy()
+        del g
+        res["error"] = np.array([smp.peer.error()])
+        res["epoch"] = np.array([int(smp.peer.header[0].item())])
+        np.savez(os.path.join(outdir, f"peer{rank}.npz"), **res)
+        smp.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_vp_fused_step_two_ranks(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_peer_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    r0, r1 = (np.load(tmp_path / f"peer{r}.npz") for r in range(world))
+    for k in r0.files:
+        assert np.array_equal(r0[k], r1[k]), k
+    assert r0["error"][0] == 0 and r0["epoch"][0] == 8    # 4 eager steps + 2 replays of 2
+    x, T, K, P, U = vp_case(41, 48, 20011)
+    want, res = oracle_ids(x, T, K, P, U)
+    near = np.array([rr.u_margin < BOUNDARY or rr.p_margin < BOUNDARY for rr in res.rows])
+    for k in ("s0", "s2", "graph0", "graph1"):
+        assert np.array_equal(r0[k][~near], want[~near]), k
+    assert np.array_equal(r0["s1"][~near[:20]], want[:20][~near[:20]])
+    assert (r0["philox"] >= 0).all()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
