@@ -427,6 +427,78 @@ def run_vocab_parallel(a):
         }), flush=True)
 
 
+def run_decode(a):
+    """configs[4] shapes: what the sampler adds to a CUDA-graph decode step.
+    Per concurrency B in {1, 8, 32, 128}: graph A = the LM head (fp16 GEMM,
+    hidden 2048 -> V 151936, random-init weights N(0, 0.02^2) as the config's
+    random-init model has, so the logits are nearly flat); graph B = the LM
+    head, then the sampler on its logits (T 0.7, top_p 0.9, as the config).
+    Added µs = B's replay time minus A's, CUDA events over graph replays.
+    The 36 transformer layers before the head are not run: they do not touch
+    the sampler's inputs, and the difference is what the sampler adds.  One
+    GPU; other ranks exit."""
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from ecahlang_b200 import sampler as S
+    H, V = 2048, 151936
+    g = torch.Generator(device=dev).manual_seed(5)
+    W = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(torch.float16)
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    per_graph = 10
+    reps = max(3, min(50, a.steps // per_graph))
+    rows = {}
+    with ClockSampler(local) as clk:
+        for B in (1, 8, 32, 128):
+            h = torch.randn(B, H, device=dev, generator=g).to(torch.float16)
+            logits = torch.empty(B, V, device=dev, dtype=torch.float16)
+            T = torch.full((B,), 0.7, device=dev)
+            K = torch.zeros(B, dtype=torch.int32, device=dev)
+            P = torch.full((B,), 0.9, device=dev)
+            smp = S.Sampler(B, V, torch.float16, dev, seed=1)
+
+            def head():
+                torch.matmul(h, W.t(), out=logits)
+
+            def step():
+                head()
+                smp(logits, T, K, P)
+
+            for _ in range(a.warmup):
+                step()
+            torch.cuda.synchronize()
+            side.wait_stream(stream)
+            times = {}
+            for name, fn in (("head", head), ("head+sampler", step)):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=side):
+                    for _ in range(per_graph):
+                        fn()
+                gr.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    gr.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                times[name] = 1e3 * e0.elapsed_time(e1) / (reps * per_graph)
+                del gr
+            rows[str(B)] = {"us_head": times["head"], "us_head_sampler": times["head+sampler"],
+                            "us_added": times["head+sampler"] - times["head"]}
+    print(json.dumps({
+        "metric": "µs the sampler adds to a CUDA-graph decode step (configs[4] shapes: LM head 2048 -> 151936 fp16)",
+        "value": rows["128"]["us_added"], "unit": "us", "higher_is_better": False, "n_gpus": 1,
+        "steps": reps * per_graph, "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "c5 decode step: LM head GEMM (+ sampler), random-init weights N(0, 0.02^2), "
+                               "T=0.7, top_p=0.9", "launch": f"CUDA-graph replays of {per_graph} steps"},
+        "per_concurrency": rows, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_flashinfer(a):
     """The reference's own GPU sampling step on the C2 inputs, for comparison
     (ecahlang/main.py:481-491; the CUDA-graph path at :356-379 does the same
@@ -526,8 +598,9 @@ def main():
                     help="reference: the CPU port of the reference path; flashinfer: the reference's "
                          "own GPU path (torch divides + FlashInfer sampling), for comparison")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["batch", "vp"], default="batch",
-                    help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split")
+    ap.add_argument("--mode", choices=["batch", "vp", "decode"], default="batch",
+                    help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split; "
+                         "decode: configs[4], µs the sampler adds to a graph-captured decode step")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="vp mode: fused kernel over NVLink peer memory, or NCCL all-gather between kernels")
     a = ap.parse_args()
@@ -538,6 +611,8 @@ def main():
         run_flashinfer(a)
     elif a.mode == "vp":
         run_vocab_parallel(a)
+    elif a.mode == "decode":
+        run_decode(a)
     else:
         run_native(a)
 

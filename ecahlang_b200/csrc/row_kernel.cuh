@@ -948,6 +948,159 @@ __device__ uint32_t radix_kth(const KParams& P, RSmem& S, int row, int R, unsign
   return (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(lb);
 }
 
+// ------------------------------------------------ dense top-p rows
+// Top-p threshold of a row without top-k whose nucleus the candidates do not
+// hold (it reaches below their floor), by two re-streams:
+//   1. the masses of the row's entries by high key byte (lane-private
+//      fixed-point sums, as the radix path's first pass) give the byte bin hb
+//      where the running mass from the top reaches p S;
+//   2. per (round, warp) segment, the masses of the entries above bin hb,
+//      and every entry of bin hb and the 32 keys below it (room for tie
+//      floors) -- the bracket [lo, hi] -- (key, index) in the candidate
+//      regions.
+// The bracket's exact per-key counts then give tau_p (the first key, from
+// hi down, where the mass above hi plus the bracket's mass from hi down
+// reaches p S), and each segment's nucleus mass (its mass above hi plus its
+// bracket entries at or above tau_p, in index order) is left in S.ss / S.sq
+// (reference M) for the segment draw, which needs no further pass.  Returns
+// false, with nothing decided, when a warp's region overflows or the
+// crossing falls outside the bracket (the fixed-point bin sums can place it
+// one bin off); the caller then takes the radix path.
+template <int DT>
+__device__ bool dense_topp(const KParams& P, RSmem& S, int row, int R, uint32_t kmax, float M, float T, float rT,
+                           float pp, float S_all, uint32_t key_cut, int& ph, uint32_t* key_lo_out) {
+  using C = Codec<DT, 16>;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float target = __fmul_rn(pp, S_all);
+  lp_zero(S);
+  stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j) {
+      const uint32_t key = ECAH_RKEY(w, j);
+      if (j < nv && key >= key_cut)
+        atomicAdd(&S.lp[((key >> 8) << 5) | static_cast<uint32_t>(lane)], to_fixed(mass_of(C::value(key), T, rT, M), kFx));
+    }
+  });
+  float* l0 = reinterpret_cast<float*>(&S.stage[0][0]);
+  if (tid < 256) {
+    unsigned long long acc = 0ull;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) acc += S.lp[(tid << 5) | ((j + tid) & 31)];
+    l0[tid] = static_cast<float>(acc) * kFxInv;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    int b;
+    float ab;
+    warp_select_seq<float, 256, true>(l0, target, &b, &ab);
+    if (lane == 0) S.ib[2] = b;
+  }
+  __syncthreads();
+  const uint32_t hb = static_cast<uint32_t>(S.ib[2]);
+  if ((hb << 8) > kmax) return false;
+  const uint32_t hi = min((hb << 8) | 255u, kmax);
+  const uint32_t lo = ((hb << 8) >= 32u) ? (hb << 8) - 32u : 0u;
+
+  // pass 2: masses above hi per segment, bracket entries into the regions
+  int fill = 0;
+  bool ovf = false;
+  const float Mq = __fmul_rn(M, kLog2e);
+  stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4* st, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+    float a = 0.f;
+    uint32_t sb = 0u;
+#pragma unroll
+    for (int j = 0; j < kEPT; ++j) {
+      const uint32_t key = ECAH_RKEY(w, j);
+      if (j < nv) {
+        if (key > hi) a += mass_of(C::value(key), T, rT, M);
+        else if (key >= lo) sb |= 1u << j;
+      }
+    }
+    a = warp_sum(a);
+    if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = Mq; }
+    const int c = __popc(sb);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+    if (fill + total > kCBW) {
+      ovf = true;
+    } else if (!ovf) {
+      const uint16_t* sr = reinterpret_cast<const uint16_t*>(st);
+      int o = warp * kCBW + fill + incl - c;
+      for (uint32_t m = sb; m; m &= m - 1u) {
+        const int j = __ffs(m) - 1;
+        S.ckey[o] = static_cast<uint16_t>(key16(sr[kEPT * lane + j]));
+        S.cidx[o] = static_cast<uint32_t>(r * kRound + kEPT * tid + j);
+        ++o;
+      }
+      fill += total;
+    }
+  });
+  if (__syncthreads_or(ovf)) return false;
+  unsigned* cnth = reinterpret_cast<unsigned*>(&S.stage[0][0]) + kCntOff;  // bin b = key hi - b
+  for (int i = tid; i < kHB; i += kT) cnth[i] = 0u;
+  fill = gather_candidates(S, fill, ph);
+  for (int i = tid; i < fill; i += kT) atomicAdd(&cnth[hi - gkey(S)[i]], 1u);
+  // mass above the bracket: the segments' sums
+  const int nseg = R * kNW;
+  const float A = rsum_f(tid < nseg ? S.ss[tid] : 0.f, S, ph);   // barrier inside: cnth complete
+  float e4[4], se = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = tid * 4 + j;
+    const unsigned cn = cnth[b];
+    e4[j] = (cn && static_cast<uint32_t>(b) <= hi - lo) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(hi - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
+    se += e4[j];
+  }
+  float btot;
+  const float exb = rscan_f(se, S, ph, &btot);
+  if (!(A < target) || !(A + btot >= target)) return false;   // the crossing lies outside the bracket
+  int mine = INT_MAX;
+  if (se > 0.f && A + exb + se >= target) {
+    float run = A + exb;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (mine == INT_MAX && e4[j] > 0.f && run + e4[j] >= target) mine = tid * 4 + j;
+      run += e4[j];
+    }
+    if (mine == INT_MAX) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (e4[j] > 0.f) mine = tid * 4 + j;
+    }
+  }
+  unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+  if (bsel == static_cast<unsigned>(INT_MAX)) {
+    // reached only after rounding: the last non-zero bin
+    int last = -1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (e4[j] > 0.f) last = tid * 4 + j;
+    bsel = static_cast<unsigned>(static_cast<int>(rmax_u(static_cast<unsigned>(last + 1), S, ph)) - 1);
+    if (bsel == 0xFFFFFFFFu) return false;
+  }
+  const uint32_t key_lo = tie_floor<DT, 16>(hi - bsel, T);
+  if (key_lo < lo) return false;
+  // each segment's bracket entries at or above key_lo, in index order
+  if (tid < nseg) {
+    const int wi = (tid & 31) * 32 + (tid >> 5);   // gather_candidates: [warp][round] counts and offsets
+    const unsigned b0 = S.lp[1024 + wi], n = S.lp[wi];
+    float add = 0.f;
+    for (unsigned i = b0; i < b0 + n; ++i) {
+      const uint32_t key = gkey(S)[i];
+      if (key >= key_lo) add += mass_of(C::value(key), T, rT, M);
+    }
+    S.ss[tid] += add;
+  }
+  __syncthreads();
+  *key_lo_out = key_lo;
+  return true;
+}
+
 // ------------------------------------------------ vocabulary-parallel local step
 // Where row `row`'s list and count go: this rank's own buffers, or, in the
 // fused step (FUSED), this rank's slot of exchange buffer h (every rank h,
@@ -1403,7 +1556,17 @@ __device__ __forceinline__ void row_body(const KParams& P) {
         }
       }
 
-      if (!fast) {
+      // rows without top-k whose nucleus reaches below the candidates
+      bool segs_ready = false;
+      if (!fast && mass_all && topp && mass_ok) {
+        uint32_t kl;
+        if (dense_topp<DT>(P, S, row, R, kmax, M, T, rT, pp, S_all, key_cut, ph, &kl)) {
+          key_lo_k = 0u;
+          key_lo = kl;
+          segs_ready = true;
+        }
+      }
+      if (!fast && !segs_ready) {
         // ---------------------------------- fallback: radix select by re-streaming
         key_lo_k = 0u;
         if (topk) key_lo_k = tie_floor<DT, 16>(radix_kth<DT>(P, S, row, R, static_cast<unsigned>(k_eff)), T);
@@ -1511,7 +1674,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       } else {
         // segment sums: from the stream (whole distribution) or a re-stream
         const int nseg = R * kNW;
-        if (!(fast && segs)) {
+        if (!(fast && segs) && !segs_ready) {
           stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
             float a = 0.f;
 #pragma unroll

@@ -119,6 +119,45 @@ def test_config3_penalised(use_mval):
     assert nb <= 1
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_dense_top_p_rows(dtype, big_batch):
+    """Rows without top-k whose nucleus is most of the row: nearly flat
+    logits (what a random-init model gives) and C3's wide Gaussian at T = 0.8.
+    The nucleus reaches below the candidates, so the threshold comes from the
+    bracket passes (or, where the bracket is too wide, the radix passes)."""
+    g = torch.Generator().manual_seed(13)
+    B, V = 24, 151936
+    x = torch.randn(B, V, generator=g) * 0.9
+    x[12:] *= 2.5 / 0.9
+    x = x.to(dtype)
+    T = np.array([0.7, 1.3, 0.7, 0.5, 0.9, 0.6] * 2 + [0.8, 0.8, 1.0, 0.6, 0.8, 1.2] * 2, np.float32)
+    K = np.zeros(B, np.int32)
+    P = np.array([0.9, 0.9, 0.5, 0.99, 0.95, 0.3] * 2 + [0.95, 0.8, 0.999, 0.3, 0.9, 0.95] * 2, np.float32)
+    U = row_uniforms(13, 0, B)
+    gpu = run_gpu(x, T, K, P, U, probs=True, tile=tiled(B) if big_batch else 1)
+    orc = run_oracle(x, T, K, P, U)
+    nb = compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
+    # with ~1e5 entries in a flat nucleus the CDF steps are ~1e-5 apart, so
+    # many rows have u or p within 1e-6 of a step; those rows still have their
+    # kept sets and probabilities checked, only their ids are exempt
+    assert nb <= B // 2
+
+
+def test_config3_repetition_only():
+    """C3's Zipf histories and parameters with the repetition penalty alone
+    (the row kernel's path; a wide nucleus at T = 0.8, p = 0.95)."""
+    w = W.config3(seed=0, B=32)
+    rp = w.rep_pen.numpy()
+    hist = [(t, c, np.array([so.penalty_divisor(int(ci), float(rp[r]), "f16") for ci in c], np.float32))
+            for r, (t, c) in enumerate(w.history)]
+    gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, history=hist, rp=rp, probs=True)
+    orc = run_oracle(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, history=hist, rp=rp)
+    nb = compare(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, gpu, orc, history=hist, rp=rp,
+                 probs=gpu[2])
+    assert nb <= 1
+
+
 def test_config1_fp32():
     w = W.config1(seed=0)
     gpu = run_gpu(w.logits, w.temperature, w.top_k, w.top_p, w.uniforms, probs=True)
