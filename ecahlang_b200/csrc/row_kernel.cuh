@@ -881,6 +881,24 @@ __device__ __forceinline__ float seg_masses(const uint32_t (&raw)[8], float T, f
   return acc.x + acc.y;
 }
 
+// mass_of(y, T, rT, M) of a thread's 16 entries (entry j in e[j]), two at a
+// time with the same roundings: q = y rT, z = q + rT (y - q T), then
+// 2^((z - M) log2e).  Padding entries (NaN) give NaN.
+template <int DT>
+__device__ __forceinline__ void masses16(const uint32_t (&raw)[8], float T, float rT, float M, float (&e)[kEPT]) {
+  const float2 rT2 = make_float2(rT, rT), nT2 = make_float2(-T, -T);
+  const float2 nM2 = make_float2(-M, -M), L2 = make_float2(kLog2e, kLog2e);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 y = vals2<DT>(raw[j]);
+    const float2 q = fmul2(y, rT2);
+    const float2 z = ffma2(ffma2(q, nT2, y), rT2, q);
+    const float2 d = fmul2(fadd2(z, nM2), L2);
+    e[2 * j] = ex2_approx(d.x);
+    e[2 * j + 1] = ex2_approx(d.y);
+  }
+}
+
 // mass of an entry relative to reference q (scaled like z): mass_of with
 // the T == 1 shortcut (z = y exactly, as the divide gives)
 __device__ __forceinline__ float emass(float y, float T, float rT, float q, bool t1) {
@@ -973,12 +991,14 @@ __device__ bool dense_topp(const KParams& P, RSmem& S, int row, int R, uint32_t 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float target = __fmul_rn(pp, S_all);
   lp_zero(S);
-  stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+  stream_row<DT>(P, S, row, 0, R, [&](int, const uint4*, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+    float e[kEPT];
+    masses16<DT>(raw, T, rT, M, e);
 #pragma unroll
     for (int j = 0; j < kEPT; ++j) {
       const uint32_t key = ECAH_RKEY(w, j);
       if (j < nv && key >= key_cut)
-        atomicAdd(&S.lp[((key >> 8) << 5) | static_cast<uint32_t>(lane)], to_fixed(mass_of(C::value(key), T, rT, M), kFx));
+        atomicAdd(&S.lp[((key >> 8) << 5) | static_cast<uint32_t>(lane)], to_fixed(e[j], kFx));
     }
   });
   float* l0 = reinterpret_cast<float*>(&S.stage[0][0]);
@@ -1005,14 +1025,16 @@ __device__ bool dense_topp(const KParams& P, RSmem& S, int row, int R, uint32_t 
   int fill = 0;
   bool ovf = false;
   const float Mq = __fmul_rn(M, kLog2e);
-  stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4* st, uint32_t (&)[8], uint32_t (&w)[8], int nv) {
+  stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+    float e[kEPT];
+    masses16<DT>(raw, T, rT, M, e);
     float a = 0.f;
     uint32_t sb = 0u;
 #pragma unroll
     for (int j = 0; j < kEPT; ++j) {
       const uint32_t key = ECAH_RKEY(w, j);
       if (j < nv) {
-        if (key > hi) a += mass_of(C::value(key), T, rT, M);
+        if (key > hi) a += e[j];
         else if (key >= lo) sb |= 1u << j;
       }
     }
