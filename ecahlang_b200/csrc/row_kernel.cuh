@@ -1231,9 +1231,24 @@ __device__ void vp_emit(const KParams& P, RSmem& S, int row, int R, int k, uint3
   if (tid == 0) vp_put_count<FUSED>(P, row, par, total);
 }
 
-// The fused step's exchange and merge of one row, after its list is out:
-// flags every rank, waits (bounded) for every rank's list of the row, then
-// merges them and draws.  Defined with the merge (vp_kernel.cuh).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Fused step, once row `row`'s list and count are stored into every rank's
+// buffer: after the CTA barrier one thread per rank fences at system scope
+// and sets the row's flag in that rank's buffer (release, system scope).
+__device__ __forceinline__ void vp_signal(const KParams& P, int row, unsigned epoch) {
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < P.vp_world) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<unsigned*>(static_cast<char*>(P.vp_base[threadIdx.x]) + P.vp_lflag) +
+                       static_cast<long long>(P.vp_rank) * P.vp_maxb + row, epoch);
+  }
+}
+
+// The fused step's wait (bounded) for every rank's list of a row, then the
+// merge and the draw.  Defined with the merge (vp_kernel.cuh).
 template <int DT>
 __device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch);
 
@@ -1278,7 +1293,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       N = static_cast<int>(min(kr, static_cast<long long>(P.V)));
       if (N > P.cand_cap) {
         if (tid == 0) vp_put_count<FUSED>(P, row, par, N);
-        if constexpr (FUSED) vp_fused_finish<DT>(P, S, row, epoch);
+        if constexpr (FUSED) vp_signal(P, row, epoch);
         __syncthreads();
         continue;
       }
@@ -1441,27 +1456,39 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     rmax2_u(best, N > 0 ? f : 0u, S, ph, &kmax, &fmax);
     if constexpr (VPL) {
       vp_emit<DT, FUSED>(P, S, row, R, N, kmax, fmax, fill, cand, ph, par);
-      if constexpr (FUSED) vp_fused_finish<DT>(P, S, row, epoch);
+      if constexpr (FUSED) vp_signal(P, row, epoch);
       __syncthreads();  // shared state is reused by the next row
       continue;
     }
     if (N > 0) f = fmax;
+    // The lowest index of the max: greedy rows and split rows need it now;
+    // sampled rows only when no entry has finite mass (see `none`), so they
+    // scan the candidates while the buffer is intact and reduce later.
     unsigned firstc = 0xFFFFFFFFu;
-    if (cand) {
-      // the max is at or above every floor: all its entries are candidates
-      for (int i = tid; i < fill; i += kT)
-        if (gkey(S)[i] == kmax) firstc = min(firstc, gidx(S)[i]);
-    } else if (best == kmax) {
-      // the lowest index of kmax among this thread's entries of round bround
-      // (fetching them for every thread ahead of the barrier measured slower)
-      const int e0 = bround * kRound + kEPT * tid;
-      float yv[kEPT];
-      load16<DT>(P, S, row, e0, yv);
+    auto scan_first = [&]() {
+      if (cand) {
+        // the max is at or above every floor: all its entries are candidates
+        for (int i = tid; i < fill; i += kT)
+          if (gkey(S)[i] == kmax) firstc = min(firstc, gidx(S)[i]);
+      } else if (best == kmax) {
+        // the lowest index of kmax among this thread's entries of round bround
+        // (fetching them for every thread ahead of the barrier measured slower)
+        const int e0 = bround * kRound + kEPT * tid;
+        float yv[kEPT];
+        load16<DT>(P, S, row, e0, yv);
 #pragma unroll
-      for (int j = 0; j < kEPT; ++j)
-        if (firstc == 0xFFFFFFFFu && e0 + j < P.V && C::from_val(yv[j]) == kmax) firstc = static_cast<unsigned>(e0 + j);
+        for (int j = 0; j < kEPT; ++j)
+          if (firstc == 0xFFFFFFFFu && e0 + j < P.V && C::from_val(yv[j]) == kmax) firstc = static_cast<unsigned>(e0 + j);
+      }
+    };
+    const bool greedy_now = !(T > 0.f) || !isfinite(__fdiv_rn(C::value(kmax), T));
+    unsigned first = 0xFFFFFFFFu;
+    if (SPLIT || greedy_now) {
+      scan_first();
+      first = rmin_u(firstc, S, ph);
+    } else if (cand) {
+      scan_first();
     }
-    unsigned first = rmin_u(firstc, S, ph);
 
     if constexpr (SPLIT) {
       PartState m{kmax, first, f, fill, overflow, cand};
@@ -1781,6 +1808,10 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       }
       if (none) {
         // no finite mass anywhere: the lowest index of the row max
+        if constexpr (!SPLIT) {
+          if (!cand) scan_first();   // from global memory: the stages may be gone
+          first = rmin_u(firstc, S, ph);
+        }
         result = static_cast<int>(first == 0xFFFFFFFFu ? 0u : first);
       }
       if (tid == 0) {
@@ -1810,6 +1841,15 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       }
     }
     __syncthreads();  // shared state is reused by the next row
+  }
+  if constexpr (FUSED) {
+    // every row of this CTA is out and flagged: now wait for the other
+    // ranks' lists of each and merge it (no rank waits before it has flagged
+    // all its own rows)
+    for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
+      vp_fused_finish<DT>(P, S, row, epoch);
+      __syncthreads();
+    }
   }
 }
 

@@ -28,15 +28,18 @@
 //             g's counts and lists, double-buffered by epoch parity.
 // Per row a CTA streams its slice, stores the list and count into its slot of
 // every rank's buffer (plain stores over NVLink, no multicast), fences at
-// system scope, sets the row's flag in every buffer (st.release.sys), waits
-// for every rank's flag in its own buffer (ld.acquire.sys, bounded by
-// vp_timeout_ns), and merges the row from its own buffer.  Ranks take rows
-// in the same order, and a row waits only on the same row of other ranks.
+// system scope and sets the row's flag in every buffer (st.release.sys).
+// Once all its rows are flagged, the CTA waits for every rank's flag of each
+// row in its own buffer (ld.acquire.sys, bounded by vp_timeout_ns) and
+// merges the row from its own buffer.  No CTA waits before it has flagged
+// all its rows, so no wait depends on another wait.
 // A rank reaches step s + 2 only after every rank has flagged every row of
 // step s + 1, which each rank does after finishing step s, so the parity
 // buffer a rank reads is never rewritten under it; flags only grow, so a
 // flag read late compares >= the epoch.
 #pragma once
+
+#include <type_traits>
 
 #include "row_kernel.cuh"
 
@@ -99,6 +102,52 @@ __device__ __forceinline__ unsigned mblock_min(unsigned v, unsigned* red) {
   for (int w = 0; w < NT / 32; ++w) m = min(m, red[w]);
   __syncthreads();
   return m;
+}
+
+// Over kWin bins in ascending order (thread t: bins t*PB .. t*PB+PB-1), the
+// first whose running sum reaches the target -- `target`, or, when frac > 0,
+// frac times the bins' sum -- and where rounding leaves it unreached, the
+// last non-zero bin; -1 when every bin is zero.  *total = the bins' sum.
+// Every thread gets the result.
+template <int NT, typename V>
+__device__ __forceinline__ int mselect(const V* hist, V target, float frac, MSmem<NT>& S, V* total) {
+  constexpr int PB = kWin / NT, NW = NT / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  V v[PB], s = V(0);
+#pragma unroll
+  for (int j = 0; j < PB; ++j) { v[j] = hist[tid * PB + j]; s += v[j]; }
+  V incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const V y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) reinterpret_cast<V*>(S.red)[warp] = incl;
+  __syncthreads();
+  V base = V(0), tot = V(0);
+  for (int w = 0; w < NW; ++w) {
+    const V x = reinterpret_cast<const V*>(S.red)[w];
+    if (w < warp) base += x;
+    tot += x;
+  }
+  *total = tot;
+  if constexpr (std::is_same<V, float>::value) {
+    if (frac > 0.f) target = __fmul_rn(frac, tot);
+  }
+  const V ex = base + incl - s;
+  int mine = INT_MAX, last = -1;
+  V acc = ex;
+#pragma unroll
+  for (int j = 0; j < PB; ++j) {
+    if (v[j] > V(0)) {
+      last = tid * PB + j;
+      if (mine == INT_MAX && acc + v[j] >= target) mine = tid * PB + j;
+    }
+    acc += v[j];
+  }
+  const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured);
+  if (pick != static_cast<unsigned>(INT_MAX)) return static_cast<int>(pick);
+  return static_cast<int>(mblock_max<NT>(static_cast<unsigned>(last + 1), S.ured)) - 1;
 }
 
 // One row of the merge by a CTA of NT threads.  `lost`: a rank's list never
@@ -165,13 +214,15 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
     const uint32_t key_cut = zero_mass_cut<DT, 16>(M, T);
     // every entry with key >= F is in the merged list: F = the highest of the
     // ranks' k-th largest keys (the lowest key of each rank's list)
-    unsigned fl = 0u;
-    if (tid < P.world) {
-      const int c = S.ofs[tid + 1] - S.ofs[tid];
-      unsigned lo = 0xFFFFFFFFu;
-      for (int i = 0; i < c; ++i) lo = min(lo, static_cast<unsigned>(S.c[S.ofs[tid] + i] >> 32));
-      fl = (c > 0) ? lo : 0u;
+    unsigned* rlo = S.cnt;   // per rank (scratch until the histogram below)
+    if (tid < P.world) rlo[tid] = 0xFFFFFFFFu;
+    __syncthreads();
+    for (int i = tid, g = 0; i < total; i += NT) {
+      while (i >= S.ofs[g + 1]) ++g;
+      atomicMin(&rlo[g], static_cast<unsigned>(S.c[i] >> 32));
     }
+    __syncthreads();
+    const unsigned fl = (tid < P.world && S.ofs[tid + 1] > S.ofs[tid]) ? rlo[tid] : 0u;
     uint32_t F = mblock_max<NT>(fl, S.ured);
     if (kmax >= static_cast<uint32_t>(kWin) && F < kmax - static_cast<uint32_t>(kWin - 1)) F = kmax - static_cast<uint32_t>(kWin - 1);
     for (int b = tid; b < kWin; b += NT) S.cnt[b] = 0u;
@@ -182,26 +233,13 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
     }
     __syncthreads();
     if (topk) {
-      if (tid < 32) {
-        unsigned tot = 0u;
-        for (int b = lane; b < kWin; b += 32) tot += S.cnt[b];
-        tot = __reduce_add_sync(0xFFFFFFFFu, tot);
-        int b; unsigned above;
-        warp_select_seq<unsigned, kWin, false>(S.cnt, static_cast<unsigned>(k_eff), &b, &above);
-        if (lane == 0) {
-          int good = tot >= static_cast<unsigned>(k_eff);
-          uint32_t klk = 0u;
-          if (good) {
-            klk = tie_floor<DT, 16>(kmax - static_cast<uint32_t>(b), T);
-            good = klk >= F;
-          }
-          S.ib[1] = good;
-          S.ib[2] = static_cast<int>(klk);
-        }
+      unsigned tot;
+      const int b = mselect<NT, unsigned>(S.cnt, static_cast<unsigned>(k_eff), 0.f, S, &tot);
+      ok = tot >= static_cast<unsigned>(k_eff) && b >= 0;
+      if (ok) {
+        key_lo_k = tie_floor<DT, 16>(kmax - static_cast<uint32_t>(b), T);   // every thread, same value
+        ok = key_lo_k >= F;
       }
-      __syncthreads();
-      ok = S.ib[1] != 0;
-      key_lo_k = static_cast<uint32_t>(S.ib[2]);
     } else {
       ok = false;  // without top-k the slices' lists do not hold the row
     }
@@ -214,17 +252,9 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
         mb[b] = (b <= bk && cn) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
       }
       __syncthreads();
-      if (tid < 32) {
-        float s = 0.f;
-        for (int b = lane; b < kWin; b += 32) s += mb[b];
-        s = warp_sum(s);
-        const float target = __fmul_rn(pp, s);
-        int b; float above;
-        warp_select_seq<float, kWin, false>(mb, target, &b, &above);
-        if (lane == 0) S.ib[3] = static_cast<int>(max(tie_floor<DT, 16>(kmax - static_cast<uint32_t>(b), T), key_lo_k));
-      }
-      __syncthreads();
-      key_lo = static_cast<uint32_t>(S.ib[3]);
+      float s;   // the top-k set's mass; the target is pp times it
+      const int b = mselect<NT, float>(mb, 0.f, pp, S, &s);
+      key_lo = max(tie_floor<DT, 16>(kmax - static_cast<uint32_t>(max(b, 0)), T), key_lo_k);
     }
     if (ok) {
       // inverse CDF over the merged entries in vocab order (thread t: a contiguous stretch)
@@ -318,9 +348,6 @@ namespace rk {
 
 constexpr unsigned kSpinMax = 1u << 24;   // backstop to the time limit of a wait
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -338,13 +365,6 @@ __device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row
   const int world = P.vp_world;
   char* own = static_cast<char*>(P.vp_base[P.vp_rank]);
   int* err = reinterpret_cast<int*>(own + 8);
-  // the row's list and count went to every rank's buffer: make them visible
-  // system-wide before any flag says so
-  __threadfence_system();
-  __syncthreads();
-  if (tid < world)
-    st_release_sys(reinterpret_cast<unsigned*>(static_cast<char*>(P.vp_base[tid]) + P.vp_lflag) +
-                       static_cast<long long>(P.vp_rank) * P.vp_maxb + row, epoch);
   int lost = 0;
   if (tid < world) {
     const unsigned* fl = reinterpret_cast<const unsigned*>(own + P.vp_lflag) + static_cast<long long>(tid) * P.vp_maxb + row;

@@ -223,6 +223,23 @@ def test_ties_and_flat_rows(dtype, big_batch):
     assert nb <= 2
 
 
+@pytest.mark.parametrize("big_batch", [False, True])
+def test_rows_without_finite_mass(big_batch):
+    """Sampled rows whose every logit is -inf have no finite z = y / T max
+    and take the greedy rule: the lowest index of the max, 0.  (The
+    reference's softmax would give NaN probabilities there; the oracle does
+    not cover such rows.)  A row with a single finite logit draws it."""
+    B, V = 6, 5000
+    x = torch.full((B, V), -float("inf")).half()
+    x[5, 17] = 2.0
+    T = np.array([1.0, 0.7, 1.0, 2.0, 1.0, 1.0], np.float32)
+    K = np.array([0, 0, 5, 0, 1, 0], np.int32)
+    P = np.array([1.0, 0.9, 1.0, 0.5, 1.0, 0.9], np.float32)
+    U = row_uniforms(8, 0, B)
+    ids, _, _ = run_gpu(x, T, K, P, U, tile=tiled(B) if big_batch else 1)
+    assert ids.tolist() == [0, 0, 0, 0, 0, 17]
+
+
 def test_many_rows_small_vocab():
     g = torch.Generator().manual_seed(21)
     B, V = 2000, 300
