@@ -1235,22 +1235,27 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Fused step, once row `row`'s list and count are stored into every rank's
-// buffer: after the CTA barrier one thread per rank fences at system scope
-// and sets the row's flag in that rank's buffer (release, system scope).
-__device__ __forceinline__ void vp_signal(const KParams& P, int row, unsigned epoch) {
+// Fused step, once the lists and counts of all this CTA's rows are stored
+// into every rank's buffer: after a CTA barrier one thread per rank fences
+// at system scope (one fence for all the rows) and sets the rows' flags in
+// that rank's buffer (release, system scope).
+__device__ __forceinline__ void vp_signal(const KParams& P, unsigned epoch) {
   __syncthreads();
   if (static_cast<int>(threadIdx.x) < P.vp_world) {
     __threadfence_system();
-    st_release_sys(reinterpret_cast<unsigned*>(static_cast<char*>(P.vp_base[threadIdx.x]) + P.vp_lflag) +
-                       static_cast<long long>(P.vp_rank) * P.vp_maxb + row, epoch);
+    unsigned* fl = reinterpret_cast<unsigned*>(static_cast<char*>(P.vp_base[threadIdx.x]) + P.vp_lflag) +
+                   static_cast<long long>(P.vp_rank) * P.vp_maxb;
+    for (int row = blockIdx.x; row < P.B; row += gridDim.x) st_release_sys(fl + row, epoch);
   }
 }
 
 // The fused step's wait (bounded) for every rank's list of a row, then the
-// merge and the draw.  Defined with the merge (vp_kernel.cuh).
+// merge and the draw, by merge group g of kMergeT threads: the CTA merges
+// kMergeGroups rows at a time.  Defined with the merge (vp_kernel.cuh).
+constexpr int kMergeT = 256;
+constexpr int kMergeGroups = kT / kMergeT;
 template <int DT>
-__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch);
+__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch, int g);
 
 // ------------------------------------------------------------ the kernel
 // One body for the sampler (VPM 0), the vocabulary-parallel local step (VPM
@@ -1293,7 +1298,6 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       N = static_cast<int>(min(kr, static_cast<long long>(P.V)));
       if (N > P.cand_cap) {
         if (tid == 0) vp_put_count<FUSED>(P, row, par, N);
-        if constexpr (FUSED) vp_signal(P, row, epoch);
         __syncthreads();
         continue;
       }
@@ -1456,7 +1460,6 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     rmax2_u(best, N > 0 ? f : 0u, S, ph, &kmax, &fmax);
     if constexpr (VPL) {
       vp_emit<DT, FUSED>(P, S, row, R, N, kmax, fmax, fill, cand, ph, par);
-      if constexpr (FUSED) vp_signal(P, row, epoch);
       __syncthreads();  // shared state is reused by the next row
       continue;
     }
@@ -1843,12 +1846,15 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     __syncthreads();  // shared state is reused by the next row
   }
   if constexpr (FUSED) {
-    // every row of this CTA is out and flagged: now wait for the other
-    // ranks' lists of each and merge it (no rank waits before it has flagged
+    // every row of this CTA is out: flag them all, then wait for the other
+    // ranks' lists of each and merge it (no CTA waits before it has flagged
     // all its own rows)
-    for (int row = blockIdx.x; row < P.B; row += gridDim.x) {
-      vp_fused_finish<DT>(P, S, row, epoch);
-      __syncthreads();
+    vp_signal(P, epoch);
+    const int g = tid / kMergeT;   // merge groups run independently from here on
+    for (int i = g;; i += kMergeGroups) {
+      const long long row = blockIdx.x + static_cast<long long>(i) * gridDim.x;
+      if (row >= P.B) break;
+      vp_fused_finish<DT>(P, S, static_cast<int>(row), epoch, g);
     }
   }
 }

@@ -27,9 +27,9 @@
 //   count     [2][world][maxb] i32 and cand [2][world][maxb][cap] u64: rank
 //             g's counts and lists, double-buffered by epoch parity.
 // Per row a CTA streams its slice, stores the list and count into its slot of
-// every rank's buffer (plain stores over NVLink, no multicast), fences at
-// system scope and sets the row's flag in every buffer (st.release.sys).
-// Once all its rows are flagged, the CTA waits for every rank's flag of each
+// every rank's buffer (plain stores over NVLink, no multicast).  Once all its
+// rows are out, the CTA fences at system scope and sets their flags in every
+// buffer (st.release.sys), then waits for every rank's flag of each
 // row in its own buffer (ld.acquire.sys, bounded by vp_timeout_ns) and
 // merges the row from its own buffer.  No CTA waits before it has flagged
 // all its rows, so no wait depends on another wait.
@@ -82,25 +82,33 @@ struct MSmem {
   float fb[8];
 };
 
+// A merge runs on a group of NT threads of the CTA (gt: the thread's index in
+// the group) that meet at hardware barrier `bar` (0 when the group is the
+// whole CTA).
 template <int NT>
-__device__ __forceinline__ unsigned mblock_max(unsigned v, unsigned* red) {
+__device__ __forceinline__ void gsync(int bar) {
+  asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(NT) : "memory");
+}
+
+template <int NT>
+__device__ __forceinline__ unsigned mblock_max(unsigned v, unsigned* red, int gt, int bar) {
   v = __reduce_max_sync(0xFFFFFFFFu, v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  if ((gt & 31) == 0) red[gt >> 5] = v;
+  gsync<NT>(bar);
   unsigned m = 0u;
   for (int w = 0; w < NT / 32; ++w) m = max(m, red[w]);
-  __syncthreads();
+  gsync<NT>(bar);
   return m;
 }
 
 template <int NT>
-__device__ __forceinline__ unsigned mblock_min(unsigned v, unsigned* red) {
+__device__ __forceinline__ unsigned mblock_min(unsigned v, unsigned* red, int gt, int bar) {
   v = __reduce_min_sync(0xFFFFFFFFu, v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
+  if ((gt & 31) == 0) red[gt >> 5] = v;
+  gsync<NT>(bar);
   unsigned m = 0xFFFFFFFFu;
   for (int w = 0; w < NT / 32; ++w) m = min(m, red[w]);
-  __syncthreads();
+  gsync<NT>(bar);
   return m;
 }
 
@@ -110,9 +118,9 @@ __device__ __forceinline__ unsigned mblock_min(unsigned v, unsigned* red) {
 // last non-zero bin; -1 when every bin is zero.  *total = the bins' sum.
 // Every thread gets the result.
 template <int NT, typename V>
-__device__ __forceinline__ int mselect(const V* hist, V target, float frac, MSmem<NT>& S, V* total) {
+__device__ __forceinline__ int mselect(const V* hist, V target, float frac, MSmem<NT>& S, V* total, int gt, int bar) {
   constexpr int PB = kWin / NT, NW = NT / 32;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = gt, lane = tid & 31, warp = tid >> 5;
   V v[PB], s = V(0);
 #pragma unroll
   for (int j = 0; j < PB; ++j) { v[j] = hist[tid * PB + j]; s += v[j]; }
@@ -123,7 +131,7 @@ __device__ __forceinline__ int mselect(const V* hist, V target, float frac, MSme
     if (lane >= o) incl += y;
   }
   if (lane == 31) reinterpret_cast<V*>(S.red)[warp] = incl;
-  __syncthreads();
+  gsync<NT>(bar);
   V base = V(0), tot = V(0);
   for (int w = 0; w < NW; ++w) {
     const V x = reinterpret_cast<const V*>(S.red)[w];
@@ -145,18 +153,19 @@ __device__ __forceinline__ int mselect(const V* hist, V target, float frac, MSme
     }
     acc += v[j];
   }
-  const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured);
+  const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured, gt, bar);
   if (pick != static_cast<unsigned>(INT_MAX)) return static_cast<int>(pick);
-  return static_cast<int>(mblock_max<NT>(static_cast<unsigned>(last + 1), S.ured)) - 1;
+  return static_cast<int>(mblock_max<NT>(static_cast<unsigned>(last + 1), S.ured, gt, bar)) - 1;
 }
 
-// One row of the merge by a CTA of NT threads.  `lost`: a rank's list never
-// arrived (the fused step's wait ran out); the row gets -1.
+// One row of the merge by a group of NT threads (gt, bar: see gsync).
+// `lost`: a rank's list never arrived (the fused step's wait ran out); the
+// row gets -1.
 template <int DT, int NT>
-__device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int row, bool lost) {
+__device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int row, bool lost, int gt, int bar) {
   constexpr int NW = NT / 32;
   using C = Codec<DT, 16>;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = gt, lane = tid & 31;
 
   // merged entries of the row: rank by rank (each rank's list is in vocab order)
   if (tid == 0) {
@@ -170,7 +179,7 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
     S.ofs[P.world] = acc;
     S.ib[0] = bad | (lost ? 1 : 0);
   }
-  __syncthreads();
+  gsync<NT>(bar);
   const int total = S.ofs[P.world];
   const bool truncated = S.ib[0] != 0;
   for (int g = 0; g < P.world; ++g) {
@@ -178,7 +187,7 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
     const unsigned long long* src = P.all_cand + (static_cast<long long>(g) * P.Bs + row) * P.cap;
     for (int i = tid; i < c; i += NT) S.c[S.ofs[g] + i] = src[i];
   }
-  __syncthreads();
+  gsync<NT>(bar);
 
   const float T = P.temperature[row];
   const int kk = P.top_k[row];
@@ -190,11 +199,11 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
   // row max and its lowest id
   unsigned km = 0u;
   for (int i = tid; i < total; i += NT) km = max(km, static_cast<unsigned>(S.c[i] >> 32));
-  const unsigned kmax = mblock_max<NT>(km, S.ured);
+  const unsigned kmax = mblock_max<NT>(km, S.ured, gt, bar);
   unsigned fid = 0xFFFFFFFFu;
   for (int i = tid; i < total; i += NT)
     if (static_cast<unsigned>(S.c[i] >> 32) == kmax) fid = min(fid, static_cast<unsigned>(S.c[i] & 0xFFFFFFFFu));
-  const unsigned first = mblock_min<NT>(fid, S.ured);
+  const unsigned first = mblock_min<NT>(fid, S.ured, gt, bar);
   const float ymax = C::value(kmax);
   const float M = __fdiv_rn(ymax, T);
   // a truncated sampled row is refused whatever its lists hold (a rank whose
@@ -216,25 +225,25 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
     // ranks' k-th largest keys (the lowest key of each rank's list)
     unsigned* rlo = S.cnt;   // per rank (scratch until the histogram below)
     if (tid < P.world) rlo[tid] = 0xFFFFFFFFu;
-    __syncthreads();
+    gsync<NT>(bar);
     for (int i = tid, g = 0; i < total; i += NT) {
       while (i >= S.ofs[g + 1]) ++g;
       atomicMin(&rlo[g], static_cast<unsigned>(S.c[i] >> 32));
     }
-    __syncthreads();
+    gsync<NT>(bar);
     const unsigned fl = (tid < P.world && S.ofs[tid + 1] > S.ofs[tid]) ? rlo[tid] : 0u;
-    uint32_t F = mblock_max<NT>(fl, S.ured);
+    uint32_t F = mblock_max<NT>(fl, S.ured, gt, bar);
     if (kmax >= static_cast<uint32_t>(kWin) && F < kmax - static_cast<uint32_t>(kWin - 1)) F = kmax - static_cast<uint32_t>(kWin - 1);
     for (int b = tid; b < kWin; b += NT) S.cnt[b] = 0u;
-    __syncthreads();
+    gsync<NT>(bar);
     for (int i = tid; i < total; i += NT) {
       const unsigned key = static_cast<unsigned>(S.c[i] >> 32);
       if (key >= F) atomicAdd(&S.cnt[kmax - key], 1u);
     }
-    __syncthreads();
+    gsync<NT>(bar);
     if (topk) {
       unsigned tot;
-      const int b = mselect<NT, unsigned>(S.cnt, static_cast<unsigned>(k_eff), 0.f, S, &tot);
+      const int b = mselect<NT, unsigned>(S.cnt, static_cast<unsigned>(k_eff), 0.f, S, &tot, gt, bar);
       ok = tot >= static_cast<unsigned>(k_eff) && b >= 0;
       if (ok) {
         key_lo_k = tie_floor<DT, 16>(kmax - static_cast<uint32_t>(b), T);   // every thread, same value
@@ -251,9 +260,9 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
         const unsigned cn = S.cnt[b];
         mb[b] = (b <= bk && cn) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
       }
-      __syncthreads();
+      gsync<NT>(bar);
       float s;   // the top-k set's mass; the target is pp times it
-      const int b = mselect<NT, float>(mb, 0.f, pp, S, &s);
+      const int b = mselect<NT, float>(mb, 0.f, pp, S, &s, gt, bar);
       key_lo = max(tie_floor<DT, 16>(kmax - static_cast<uint32_t>(max(b, 0)), T), key_lo_k);
     }
     if (ok) {
@@ -278,7 +287,7 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
         if (lane >= o) incl += y;
       }
       if (lane == 31) S.red[tid >> 5] = incl;
-      __syncthreads();
+      gsync<NT>(bar);
       float base = 0.f, tot = 0.f;
       for (int w = 0; w < NW; ++w) {
         if (w < (tid >> 5)) base += S.red[w];
@@ -299,9 +308,9 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
         }
         if (mine == INT_MAX) mine = lastp;
       }
-      __syncthreads();
-      const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured);
-      const unsigned last = mblock_max<NT>(static_cast<unsigned>(lastp + 1), S.ured);
+      gsync<NT>(bar);
+      const unsigned pick = mblock_min<NT>(static_cast<unsigned>(mine), S.ured, gt, bar);
+      const unsigned last = mblock_max<NT>(static_cast<unsigned>(lastp + 1), S.ured, gt, bar);
       if (pick != static_cast<unsigned>(INT_MAX)) result = static_cast<int>(S.c[pick] & 0xFFFFFFFFu);
       else if (last > 0u) result = static_cast<int>(S.c[last - 1u] & 0xFFFFFFFFu);
       else ok = false;
@@ -338,7 +347,7 @@ __device__ __forceinline__ void merge_row(const VParams& P, MSmem<NT>& S, int ro
 template <int DT>
 __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ VParams P) {
   __shared__ MSmem<kMT> S;
-  merge_row<DT, kMT>(P, S, blockIdx.x, false);
+  merge_row<DT, kMT>(P, S, blockIdx.x, false, threadIdx.x, 0);
 }
 
 }  // namespace vp
@@ -347,6 +356,8 @@ __global__ void __launch_bounds__(kMT) vp_merge_kernel(const __grid_constant__ V
 namespace rk {
 
 constexpr unsigned kSpinMax = 1u << 24;   // backstop to the time limit of a wait
+static_assert(kMergeGroups * sizeof(vp::MSmem<kMergeT>) <= sizeof(RSmem::stage) + sizeof(RSmem::lp),
+              "merge scratch of the fused step must fit in the stages and the histogram scratch");
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;
@@ -360,8 +371,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 template <int DT>
-__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch) {
-  const int tid = threadIdx.x;
+__device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row, unsigned epoch, int g) {
+  // group g (threads 256 g .. 256 g + 255, hardware barrier 1 + g) and its
+  // own merge scratch, carved from the stages and the histogram scratch
+  constexpr int NT = kMergeT;
+  const int tid = threadIdx.x - NT * g, bar = 1 + g;
+  vp::MSmem<NT>& M_S = reinterpret_cast<vp::MSmem<NT>*>(&S.stage[0][0])[g];
   const int world = P.vp_world;
   char* own = static_cast<char*>(P.vp_base[P.vp_rank]);
   int* err = reinterpret_cast<int*>(own + 8);
@@ -383,7 +398,11 @@ __device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row
       }
     }
   }
-  lost = __syncthreads_or(lost);
+  if (tid == 0) M_S.ib[5] = 0;
+  vp::gsync<NT>(bar);
+  if (lost) M_S.ib[5] = 1;
+  vp::gsync<NT>(bar);
+  lost = M_S.ib[5];
   vp::VParams M;
   M.B = P.B; M.V = P.vocab_total; M.Bs = P.vp_maxb;
   M.temperature = P.temperature; M.top_k = P.top_k; M.top_p = P.top_p;
@@ -395,8 +414,8 @@ __device__ __noinline__ void vp_fused_finish(const KParams& P, RSmem& S, int row
   M.done_counter = reinterpret_cast<unsigned*>(own + 4);
   M.epoch = reinterpret_cast<unsigned*>(own);
   M.out = P.out; M.row_stats = P.row_stats;
-  // the stages are free once every thread has stored its part of the list
-  vp::merge_row<DT, kT>(M, *reinterpret_cast<vp::MSmem<kT>*>(&S.stage[0][0]), row, lost != 0);
+  vp::merge_row<DT, NT>(M, M_S, row, lost != 0, tid, bar);
+  vp::gsync<NT>(bar);   // the group's scratch is reused by its next row
 }
 
 // The whole vocabulary-parallel step for this rank: stream, local list into
