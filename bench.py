@@ -499,6 +499,77 @@ def run_decode(a):
     }), flush=True)
 
 
+def run_c3(a):
+    """B=128, V=151936 fp16, Zipf histories, T 0.8, top-p 0.95.
+    Two lines of one JSON object: the repetition penalty alone (the row
+    kernel; a wide nucleus, so the dense top-p path) and repetition +
+    frequency + presence penalties (the cluster kernel, 32-bit keys).  CUDA-
+    graph replays over rotating input copies, CUDA events.  One GPU; other
+    ranks exit."""
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from ecahlang_b200 import sampler as S
+    from ecahlang_b200 import workloads as W
+    w = W.config3(seed=0)
+    B, V = w.batch, w.vocab
+    bytes_in = B * V * 2
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits.to(dev) for _ in range(nbuf)]
+    T, K, P, U = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev), w.uniforms.to(dev)
+    cap = max(len(t) for t, _ in w.history)
+    pen = S.PenaltyState(B, cap, torch.float16, dev)
+    for r, (t, c) in enumerate(w.history):
+        pen.load(r, t, c, None)
+    row_slot = torch.arange(B, dtype=torch.int32, device=dev)
+    rf = torch.as_tensor(S.repetition_factor(w.rep_pen.numpy()), dtype=torch.float32).to(dev)
+    fp, pp = w.freq_pen.to(dev), w.pres_pen.to(dev)
+    wsb = S.new_workspace(B, V, torch.float16, dev)
+    out = torch.zeros(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    chunk = min(a.steps, 2 * nbuf)
+    reps = max(1, a.steps // chunk)
+
+    def timed(fn):
+        for i in range(a.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        side.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(chunk):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return 1e3 * e0.elapsed_time(e1) / (reps * chunk)
+
+    with ClockSampler(local) as clk:
+        us_rp = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
+                                         penalty=pen, row_slot=row_slot))
+        us_all = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
+                                          freq_pen=fp, pres_pen=pp, penalty=pen, row_slot=row_slot,
+                                          freq_pres=True))
+    print(json.dumps({
+        "metric": "penalised sampling step (configs[2]: B=128, V=151936 fp16, T 0.8, top-p 0.95)",
+        "value": us_rp, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": reps * chunk,
+        "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "c3_penalised B=128 V=151936 fp16, 384-token Zipf histories",
+                   "launch": f"CUDA-graph replays of {chunk} launches", "l2": f"{nbuf} rotating input copies"},
+        "us_repetition_only": us_rp, "us_repetition_frequency_presence": us_all,
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_flashinfer(a):
     """The reference's own GPU sampling step on the C2 inputs, for comparison
     (ecahlang/main.py:481-491; the CUDA-graph path at :356-379 does the same
@@ -598,9 +669,10 @@ def main():
                     help="reference: the CPU port of the reference path; flashinfer: the reference's "
                          "own GPU path (torch divides + FlashInfer sampling), for comparison")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["batch", "vp", "decode"], default="batch",
+    ap.add_argument("--mode", choices=["batch", "vp", "decode", "c3"], default="batch",
                     help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split; "
-                         "decode: configs[4], µs the sampler adds to a graph-captured decode step")
+                         "decode: configs[4], µs the sampler adds to a graph-captured decode step; "
+                         "c3: configs[2], the penalised step")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="vp mode: fused kernel over NVLink peer memory, or NCCL all-gather between kernels")
     a = ap.parse_args()
@@ -613,6 +685,8 @@ def main():
         run_vocab_parallel(a)
     elif a.mode == "decode":
         run_decode(a)
+    elif a.mode == "c3":
+        run_c3(a)
     else:
         run_native(a)
 
