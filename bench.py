@@ -122,22 +122,65 @@ def _dist():
     return ws, rank, local
 
 
-def cpu_reference_rows_per_sec(w, target_s: float = 0.5, max_rows=None):
-    """Time the torch-CPU port of the reference path on a bounded sample."""
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def _all_cores():
+    """Give torch every host core (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_reference_step(w):
+    """One full step of the torch-CPU port of the reference path over every
+    row of the workload, on all host cores; returns (rows, threads, step)."""
     from oracle.torch_port import sample_batch_torch
-    threads = torch.get_num_threads()
-    rows = 8
-    # the row groups are contiguous blocks of B/4 rows: take rows group-interleaved
-    # (0, q, 2q, 3q, 1, q+1, ...) so any prefix of the sample mixes all four groups
-    q = max(w.batch // 4, 1)
-    order = torch.tensor(sorted(range(w.batch), key=lambda r: (r % q, r // q)))
-    sub = [t[order] for t in (w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)]
-    args = lambda n: tuple(t[:n] for t in sub)
-    t0 = time.perf_counter()
-    sample_batch_torch(*args(rows))
-    dt = time.perf_counter() - t0
-    rows = max(1, min(w.batch if max_rows is None else max_rows, int(rows * target_s / max(dt, 1e-3))))
-    return rows, threads, lambda: sample_batch_torch(*args(rows))
+    threads = _all_cores()
+    args = (w.logits, w.temperature, w.top_k, w.top_p, w.uniforms)
+    return w.batch, threads, lambda: sample_batch_torch(*args)
+
+
+def reference_logits_to_probs_c1(budget_s: float = 10.0):
+    """The reference's own CPU sampler, ecahlang.utils.logits_to_probs
+    (ecahlang/utils.py:3-18), run as-is on configs[0] (B=8, V=151936 fp32,
+    T 0.7, k 50; it has no top-p stage) from the installed copy of the
+    reference in baseline/_ref.  Returns a dict for the JSON line."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "ecahlang")):
+        return {"unavailable": "baseline/_ref holds no installed reference"}
+    if ref not in sys.path:
+        sys.path.append(ref)
+    from ecahlang.utils import logits_to_probs
+    from ecahlang_b200 import workloads as W
+    threads = _all_cores()
+    w = W.config1(seed=0)
+    B = w.batch
+    mask = torch.ones_like(w.logits)
+    T = w.temperature.reshape(B, 1)
+    K = w.top_k.long()
+    P = w.top_p
+    with torch.no_grad():
+        logits_to_probs(w.logits, mask, T, K, P)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            logits_to_probs(w.logits, mask, T, K, P)
+            n += 1
+        dt = time.perf_counter() - t0
+    return {"value": B * n / dt, "unit": "rows/s", "ms_per_call": 1e3 * dt / n, "calls": n, "cores": threads,
+            "cpu_model": _cpu_model(),
+            "workload": "configs[0]: B=8, V=151936 fp32 N(0,3^2) + 5 spikes at +12, T 0.7, k 50 "
+                        "(logits_to_probs has no top-p)",
+            "kind": "reference", "source": "ecahlang.utils.logits_to_probs from baseline/_ref, unmodified"}
 
 
 def run_reference(a):
@@ -146,27 +189,34 @@ def run_reference(a):
         return
     from ecahlang_b200 import workloads as W
     w = W.config2(seed=0)
-    # size each step so the whole --steps/--warmup run stays near two minutes of CPU work
-    per_step = min(0.25, max(0.005, 120.0 / (a.steps + a.warmup)))
-    rows, threads, step = cpu_reference_rows_per_sec(w, target_s=per_step)
-    for _ in range(a.warmup):
+    rows, threads, step = cpu_reference_step(w)
+    t0 = time.perf_counter()
+    step()
+    t1 = time.perf_counter() - t0
+    # every step is the whole 128-row batch; the number of timed steps is
+    # capped so the run stays near two minutes of CPU work
+    steps = max(1, min(a.steps, int(90.0 / max(t1, 1e-3))))
+    warm = max(1, min(a.warmup, int(15.0 / max(t1, 1e-3))))
+    for _ in range(warm):
         step()
     t0 = time.perf_counter()
-    for _ in range(a.steps):
+    for _ in range(steps):
         step()
     dt = time.perf_counter() - t0
-    rps = rows * a.steps / dt
-    sample = (f"{rows} of the 128 rows per step, taken group-interleaved (rows 0, 32, 64, 96, 1, 33, ...) "
-              f"so all four row groups are equally represented")
+    rps = rows * steps / dt
+    sample = (f"all {rows} rows of the workload per step; {steps} timed steps of the {a.steps} requested "
+              f"(capped to about 90 s of CPU time), {warm} warm-up steps")
     line = {
         "impl": "reference", "metric": METRIC, "value": rps, "unit": "rows/s", "n_gpus": a.gpus,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * dt / a.steps,
+        "steps": steps, "steps_requested": a.steps, "warmup": warm, "ms_per_step": 1e3 * dt / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic",
-        "config": {"workload": "c2_mixed B=128 V=151936 fp16 (bounded row sample per step)",
-                   "batch": 128, "vocab": 151936, "parallelism": "cpu"},
-        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": "c2_mixed B=128 V=151936 fp16 (configs[1])", "batch": 128, "vocab": 151936,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": rps, "unit": "rows/s", "cores": threads, "cpu_model": _cpu_model(),
+                         "kind": "port", "sample": sample},
         "e2e": {"value": rps, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_logits_to_probs_c1": reference_logits_to_probs_c1(),
     }
     print(json.dumps(line), flush=True)
 
@@ -298,18 +348,20 @@ def run_native(a):
             "clocks": clk.summary(),
         }
         if ws == 1 and not a.no_cpu_baseline:
-            rows, threads, cstep = cpu_reference_rows_per_sec(w, target_s=2.0)
+            rows, threads, cstep = cpu_reference_step(w)
             cstep()
             t0 = time.perf_counter()
             n = 0
-            while time.perf_counter() - t0 < 10.0:
+            while time.perf_counter() - t0 < 15.0:
                 cstep()
                 n += 1
             dt = time.perf_counter() - t0
             line["cpu_baseline"] = {
-                "value": rows * n / dt, "unit": "rows/s", "cores": threads, "kind": "port",
-                "sample": f"{rows} group-interleaved rows of the workload, {n} repetitions in {dt:.1f} s "
-                          f"(torch CPU port of the reference path, {threads} threads)"}
+                "value": rows * n / dt, "unit": "rows/s", "cores": threads, "cpu_model": _cpu_model(),
+                "kind": "port",
+                "sample": f"all {rows} rows of the workload, {n} steps in {dt:.1f} s "
+                          f"(torch CPU port of the reference path, {threads} threads)",
+                "reference_logits_to_probs_c1": reference_logits_to_probs_c1()}
     del g_full, g_rem
     if ws > 1:
         torch.distributed.barrier()

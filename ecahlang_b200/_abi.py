@@ -24,7 +24,8 @@ EXPORTS = ("ecah_sampler_abi_version", "ecah_status_string", "ecah_sampler_works
            "ecah_sampler_launch", "ecah_hist_update", "ecah_philox_uniforms",
            "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes",
            "ecah_vp_local", "ecah_vp_merge", "ecah_vp_exchange_bytes", "ecah_vp_step",
-           "ecah_vp_ipc_alloc", "ecah_vp_ipc_open", "ecah_vp_ipc_close", "ecah_vp_ipc_free")
+           "ecah_vp_ipc_alloc", "ecah_vp_ipc_open", "ecah_vp_ipc_close", "ecah_vp_ipc_free",
+           "ecah_quotient_mismatches")
 IPC_HANDLE_BYTES = 64
 
 
@@ -112,6 +113,8 @@ def lib():
         L.ecah_vp_ipc_close.argtypes = [c_void_p]
         L.ecah_vp_ipc_free.restype = c_int32
         L.ecah_vp_ipc_free.argtypes = [c_void_p]
+        L.ecah_quotient_mismatches.restype = c_int32
+        L.ecah_quotient_mismatches.argtypes = [c_int32, c_void_p, c_int32, c_void_p, c_void_p]
         if L.ecah_sampler_abi_version() != ABI_VERSION:
             raise EcahError("libecah_sampler.so ABI version mismatch")
         _lib = L

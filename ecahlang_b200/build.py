@@ -19,7 +19,7 @@ LIB = os.path.join(LIB_DIR, "libecah_sampler.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
          "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]
-SOURCES = ["sampler.cu", "noalloc.cu"]
+SOURCES = ["sampler.cu", "noalloc.cu", "diag.cu"]
 
 
 def _nvcc() -> str:

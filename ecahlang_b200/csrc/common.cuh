@@ -125,6 +125,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// y / T from the reciprocal rT = __frcp_rn(T) with one correction step
+// (Markstein, "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990): q = RN(y rT), r = RN(y - q T)
+// (exact through the fma), q' = RN(q + r rT).  ecah_quotient_mismatches
+// compares it with the IEEE quotient over every fp16 and bf16 input and over
+// every float32 input, per temperature.
+__device__ __forceinline__ float quot_rn(float y, float T, float rT) {
+  const float q = __fmul_rn(y, rT);
+  return __fmaf_rn(__fmaf_rn(-q, T, y), rT, q);
+}
+
 // Unnormalised softmax mass of a token whose (penalised) logit is y:
 // z = y / T rounded to float32 exactly as torch's divide, then exp(z - M).
 __device__ __forceinline__ float token_mass(float y, float T, float M) {

@@ -35,7 +35,8 @@ class SamplingManager:
     """Slot-indexed penalty histories plus the step's sampling buffers."""
 
     def __init__(self, vocab_size: int, seq_lens: int = 128, dtype: torch.dtype = torch.float16,
-                 device="cuda", history_capacity: int = 1024, seed: int = 0):
+                 device="cuda", history_capacity: int = 1024, seed: int = 0,
+                 freq_pres_in_graphs: bool = False):
         self.vocab_size = vocab_size
         self.seq_lens = max(seq_lens, 128)                      # manager.py:31
         self.dtype = dtype
@@ -47,6 +48,16 @@ class SamplingManager:
         self.philox_state = new_philox_state(seed, 0, self.device)
         self._fp_eager = False                                  # any frequency/presence penalty filled
         self._fp_cg: Dict[int, bool] = {}
+        # Whether a bucket's sampler was captured into a CUDA graph with the
+        # frequency/presence penalties on: a graph replays the launch it
+        # captured, so a bucket captured without them cannot take them later.
+        # freq_pres_in_graphs=True captures every bucket with them.
+        self.freq_pres_in_graphs = freq_pres_in_graphs
+        self._cg_captured_fp: Dict[int, bool] = {}
+        # overflow flags of the slot histories, copied to the host after every
+        # update and checked when the next step's parameters are filled (the
+        # host has read the previous step's ids by then)
+        self._overflow_host = _pinned(torch.zeros(self.seq_lens, dtype=torch.int32))
 
     # ------------------------------------------------------------------ slots
     def allocate(self, batch_id) -> int:
@@ -57,6 +68,7 @@ class SamplingManager:
         seq_len = self.free_seq_lens.pop()
         self.batch_to_seq_len[batch_id] = seq_len
         self.penalty.reset(seq_len)
+        self._overflow_host[seq_len] = 0
         return seq_len
 
     def free(self, batch_id) -> None:
@@ -68,7 +80,13 @@ class SamplingManager:
     def _slots(self, batch_ids: Optional[Sequence]) -> Optional[np.ndarray]:
         if batch_ids is None:
             return None
-        return np.array([self.batch_to_seq_len[b] for b in batch_ids], dtype=np.int32)
+        slots = np.array([self.batch_to_seq_len[b] for b in batch_ids], dtype=np.int32)
+        full = [int(s) for s in slots if self._overflow_host[int(s)]]
+        if full:
+            raise RuntimeError(
+                f"penalty history of slot(s) {full} is full ({self.penalty.capacity} distinct tokens): "
+                "later tokens would go unpenalised; raise history_capacity")
+        return slots
 
     # ------------------------------------------------------- eager buffers
     def init_sampling_buffers(self, max_batch_size: int) -> None:
@@ -158,7 +176,12 @@ class SamplingManager:
         self._cg_freq[bs].fill_(0.0)
         self._cg_pres[bs].fill_(0.0)
         self._cg_slot[bs].fill_(-1)
-        self._fp_cg[bs] = self._write_host(n, temperatures, top_ks, top_ps, rep_pens, freq_pens, pres_pens, batch_ids)
+        fp = self._write_host(n, temperatures, top_ks, top_ps, rep_pens, freq_pens, pres_pens, batch_ids)
+        if fp and self._cg_captured_fp.get(bs) is False:
+            raise RuntimeError(
+                f"bucket {bs} was captured into a CUDA graph without frequency/presence penalties; "
+                "a replay cannot apply them (construct the manager with freq_pres_in_graphs=True)")
+        self._fp_cg[bs] = fp
         for g, c in ((self._cg_temperature[bs], self.sampling_temperature_cpu),
                      (self._cg_top_k[bs], self.sampling_top_k_cpu),
                      (self._cg_top_p[bs], self.sampling_top_p_cpu),
@@ -188,6 +211,10 @@ class SamplingManager:
         if bucket_size is not None and B != bucket_size:
             raise RuntimeError(f"bucket {bucket_size} needs {bucket_size} logits rows, got {B}")
         T, K, P, rep, freq, pres, slot, out, fp = self._buffers(B, bucket_size)
+        if bucket_size is not None:
+            fp = fp or self.freq_pres_in_graphs
+            if torch.cuda.is_current_stream_capturing():
+                self._cg_captured_fp[bucket_size] = fp
         if self._workspace is None:
             self._workspace = new_workspace(self.max_batch_size, self.vocab_size, self.dtype, self.device)
         return launch(logits, T.view(-1), K, P, out, self._workspace,
@@ -202,3 +229,4 @@ class SamplingManager:
         B = ids.numel()
         _, _, _, rep, _, _, slot, _, _ = self._buffers(B, bucket_size)
         self.penalty.update(ids.view(-1)[:B], slot[:B], rep[:B])
+        self._overflow_host.copy_(self.penalty.overflow, non_blocking=True)

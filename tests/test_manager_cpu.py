@@ -76,3 +76,36 @@ def test_sample_has_no_cpu_path():
     m.fill_sampling_params(2, [1.0, 1.0], [V, V], [1.0, 1.0])
     with pytest.raises(RuntimeError, match="CUDA"):
         m.sample(torch.zeros(2, V, dtype=torch.float16))
+
+
+def test_bucket_captured_without_additive_penalties_refuses_them():
+    """A CUDA graph replays the launch it captured: a bucket captured with the
+    frequency/presence penalties off must refuse them later, loudly."""
+    m = _mgr()
+    m.init_cuda_graph_buffers([2, 4])
+    m._cg_captured_fp[2] = False          # what sample() records while capturing
+    m.fill_cuda_graph_sampling_params(2, 1, [1.0], [V], [1.0])            # none requested: fine
+    with pytest.raises(RuntimeError, match="captured"):
+        m.fill_cuda_graph_sampling_params(2, 1, [1.0], [V], [1.0], freq_pens=[0.5])
+    m.fill_cuda_graph_sampling_params(4, 1, [1.0], [V], [1.0], freq_pens=[0.5])   # never captured
+    m2 = SamplingManager(V, seq_lens=8, dtype=torch.float16, device="cpu", history_capacity=16,
+                         freq_pres_in_graphs=True)
+    m2.init_sampling_buffers(8)
+    m2.init_cuda_graph_buffers([2])
+    m2._cg_captured_fp[2] = True
+    m2.fill_cuda_graph_sampling_params(2, 1, [1.0], [V], [1.0], pres_pens=[0.3])
+
+
+def test_full_penalty_history_is_reported():
+    """A slot whose history filled up (overflow flag copied back after the
+    update) makes the next fill for that request raise."""
+    m = _mgr()
+    s = m.allocate("r")
+    m.fill_sampling_params(1, [1.0], [V], [1.0], rep_pens=[1.1], batch_ids=["r"])
+    m._overflow_host[s] = 1               # what update_penalties copies back
+    with pytest.raises(RuntimeError, match="full"):
+        m.fill_sampling_params(1, [1.0], [V], [1.0], rep_pens=[1.1], batch_ids=["r"])
+    m.free("r")
+    s2 = m.allocate("r2")
+    assert s2 == s
+    m.fill_sampling_params(1, [1.0], [V], [1.0], rep_pens=[1.1], batch_ids=["r2"])   # reset on allocate
