@@ -9,9 +9,10 @@
 
 namespace ecah {
 
-// counts[2 t]: finite inputs whose quotient differs in value from the IEEE
-// quotient while that quotient is a normal float32 (|q| >= 2^-126);
-// counts[2 t + 1]: the other differences (the sign of a zero, subnormal
+// Per temperature t, over finite inputs whose IEEE quotient is a normal
+// float32 (|q| >= 2^-126): counts[3 t] = quotients more than one unit in the
+// last place away from it, counts[3 t + 1] = quotients exactly one unit away;
+// counts[3 t + 2] = the other differences (the sign of a zero, subnormal
 // quotients, non-finite inputs), which the masses never see: a subnormal z
 // lies 87 or more below any row max of a sampled row.
 template <int DT>
@@ -21,7 +22,7 @@ __global__ void quotient_check_kernel(const float* T, int nT, unsigned long long
   for (int t = 0; t < nT; ++t) {
     const float Tv = T[t];
     const float rT = __frcp_rn(Tv);
-    unsigned long long bad = 0, other = 0;
+    unsigned long long bad = 0, ulp1 = 0, other = 0;
     for (unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += stride) {
       const float y = DType<DT>::to_f32(static_cast<uint32_t>(i));
@@ -30,14 +31,21 @@ __global__ void quotient_check_kernel(const float* T, int nT, unsigned long long
       if (__float_as_uint(a) == __float_as_uint(b)) continue;
       if (a != a && b != b) continue;   // both NaN
       const bool normal = isfinite(y) && fabsf(b) >= 1.17549435e-38f && isfinite(b);
-      if (normal && a != b) ++bad;
-      else ++other;
+      if (normal && a != b) {
+        const int d = static_cast<int>(__float_as_uint(a)) - static_cast<int>(__float_as_uint(b));
+        if (d == 1 || d == -1) ++ulp1;
+        else ++bad;
+      } else {
+        ++other;
+      }
     }
     bad = __reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(bad));
+    ulp1 = __reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(ulp1));
     other = __reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(other));
     if ((threadIdx.x & 31) == 0) {
-      if (bad) atomicAdd(&counts[2 * t], bad);
-      if (other) atomicAdd(&counts[2 * t + 1], other);
+      if (bad) atomicAdd(&counts[3 * t], bad);
+      if (ulp1) atomicAdd(&counts[3 * t + 1], ulp1);
+      if (other) atomicAdd(&counts[3 * t + 2], other);
     }
   }
 }
@@ -52,7 +60,7 @@ extern "C" int ecah_quotient_mismatches(int32_t dtype, const float* temperature,
   if (n_temperature == 0) return ECAH_OK;
   if (!temperature || !counts) return ECAH_ERR_NULL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(counts, 0, sizeof(unsigned long long) * 2 * n_temperature, s) != cudaSuccess)
+  if (cudaMemsetAsync(counts, 0, sizeof(unsigned long long) * 3 * n_temperature, s) != cudaSuccess)
     return ECAH_ERR_LAUNCH;
   switch (dtype) {
     case ECAH_DTYPE_F16: quotient_check_kernel<ECAH_DTYPE_F16><<<64, 1024, 0, s>>>(temperature, n_temperature, counts); break;

@@ -166,13 +166,14 @@ ECAH_API int ecah_sampler_launch_noalloc(const ecah_sampler_args* args, void* st
 ECAH_API size_t ecah_sampler_noalloc_scratch_bytes(void);
 
 /* Diagnostic; no counterpart in the reference.  For each of the n_temperature
- * device temperatures T[t], counts the inputs y of `dtype` (every fp16 or bf16
- * bit pattern, or every float32 bit pattern) whose y / T as the kernels compute
- * it for softmax masses (reciprocal plus one correction step) differs from the
- * IEEE float32 quotient torch computes for `logits / temperature`
- * (ecahlang/main.py:170).  counts (device, 2 * n_temperature entries):
- * counts[2t] = finite inputs whose IEEE quotient is a normal float32,
- * counts[2t+1] = the rest (zero signs, subnormal quotients, non-finite
+ * device temperatures T[t], compares y / T as the kernels compute it for
+ * softmax masses (reciprocal plus one correction step) with the IEEE float32
+ * quotient torch computes for `logits / temperature` (ecahlang/main.py:170),
+ * over every input y of `dtype` (every fp16 or bf16 bit pattern, or every
+ * float32 bit pattern).  counts (device, 3 * n_temperature entries), over
+ * finite inputs whose IEEE quotient is a normal float32: counts[3t] = more
+ * than one unit in the last place apart, counts[3t+1] = exactly one unit
+ * apart; counts[3t+2] = the rest (zero signs, subnormal quotients, non-finite
  * inputs).  A float32 sweep takes a few milliseconds per temperature. */
 ECAH_API int ecah_quotient_mismatches(int32_t dtype, const float* temperature, int32_t n_temperature,
                                       unsigned long long* counts, void* stream);

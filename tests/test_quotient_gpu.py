@@ -2,10 +2,18 @@
 
 The reference divides the penalised logits by the temperature with torch
 (``logits / temperature``, ecahlang/main.py:170), an IEEE float32 divide.  The
-kernels compute masses from ``quot_rn`` (the reciprocal of T and one
+fp16 kernels compute masses from ``quot_rn`` (the reciprocal of T and one
 correction step) instead of a divide per entry.  These tests run every input
-of each dtype through both on the device, over a spread of temperatures, and
-require equal values wherever the IEEE quotient is a normal float32.
+of each dtype through both on the device, over a spread of temperatures:
+
+- fp16: equal to the IEEE quotient for every input whose quotient is a
+  normal float32, at every temperature (so fp16 masses are exact);
+- bf16 and float32: never more than one unit in the last place away, and a
+  one-unit difference does occur for a fraction of a percent of the inputs
+  at most temperatures.  A one-unit change of z moves that entry's mass by
+  about |z| * 2^-23 relative (below 1e-5 for |z| < 80), inside the
+  probability tolerance; thresholds are keys, compared with the IEEE divide
+  for every dtype, so kept sets do not depend on it.
 """
 from __future__ import annotations
 
@@ -30,27 +38,35 @@ def _temperatures():
 def _mismatches(dtype, temps):
     dev = torch.device("cuda")
     T = torch.as_tensor(temps, dtype=torch.float32, device=dev)
-    counts = torch.zeros(2 * len(temps), dtype=torch.int64, device=dev)
+    counts = torch.zeros(3 * len(temps), dtype=torch.int64, device=dev)
     st = _abi.lib().ecah_quotient_mismatches(dtype, ctypes.c_void_p(T.data_ptr()), len(temps),
                                              ctypes.c_void_p(counts.data_ptr()),
                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _abi.check(st, "ecah_quotient_mismatches")
     torch.cuda.synchronize()
-    return counts.cpu().numpy().reshape(-1, 2)
+    return counts.cpu().numpy().reshape(-1, 3)
 
 
-@pytest.mark.parametrize("dtype", [_abi.DTYPE_F16, _abi.DTYPE_BF16])
-def test_sixteen_bit_inputs_divide_exactly(dtype):
+def test_fp16_inputs_divide_exactly():
     temps = _temperatures()
-    c = _mismatches(dtype, temps)
-    bad = {float(t): int(n) for t, n in zip(temps, c[:, 0]) if n}
+    c = _mismatches(_abi.DTYPE_F16, temps)
+    bad = {float(t): (int(a), int(b)) for t, a, b in zip(temps, c[:, 0], c[:, 1]) if a or b}
     assert not bad, f"quotients differ from the IEEE divide at T: {bad}"
 
 
-def test_float32_inputs_divide_exactly():
+def test_bf16_inputs_stay_within_one_ulp():
+    temps = _temperatures()
+    c = _mismatches(_abi.DTYPE_BF16, temps)
+    assert not c[:, 0].any(), "a bf16 quotient is more than one ulp from the IEEE divide"
+    # the one-ulp differences are why the bf16 paths use the IEEE divide
+    assert c[:, 1].sum() > 0
+
+
+def test_float32_inputs_stay_within_one_ulp():
     # every float32 bit pattern, at a smaller set of temperatures (each sweep
     # is 2^32 quotients)
     temps = np.asarray([1e-5, 0.5, 0.7, 0.8, 1.0, 1.1, 1.2, 3.0, 0.6180339887, 0.9134], dtype=np.float32)
     c = _mismatches(_abi.DTYPE_F32, temps)
-    bad = {float(t): int(n) for t, n in zip(temps, c[:, 0]) if n}
-    assert not bad, f"quotients differ from the IEEE divide at T: {bad}"
+    assert not c[:, 0].any(), "a float32 quotient is more than one ulp from the IEEE divide"
+    # powers of two divide exactly
+    assert c[list(temps).index(np.float32(1.0)), 1] == 0 and c[list(temps).index(np.float32(0.5)), 1] == 0
