@@ -30,6 +30,9 @@
 // cluster kernel (sampler_kernel.cuh).
 #pragma once
 
+#include <cstddef>
+#include <type_traits>
+
 #include "stream_kernel.cuh"
 
 namespace ecah {
@@ -332,13 +335,9 @@ __device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], 
   for (int j = 0; j < 8; ++j) w[j] = keys2(raw[j]);
 }
 
-// entries e0 .. e0+15 of the row read from global memory with the
-// repetition-penalty patch applied (NaN past the row end)
+// the repetition-penalty patch of entries e0 .. e0+15 (values in yv)
 template <int DT>
-__device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
-#pragma unroll
-  for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
+__device__ void patch16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
   if (!row_has_penalty(P, row)) return;
   auto patch = [&](int li, float m) {
 #pragma unroll
@@ -364,6 +363,38 @@ __device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float 
     const int cn = P.hist_cnt[hb + h];
     if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
     patch(li, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf));
+  }
+}
+
+// entries e0 .. e0+15 of the row read from global memory with the
+// repetition-penalty patch applied (NaN past the row end)
+template <int DT>
+__device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
+  patch16<DT>(P, S, row, e0, yv);
+}
+
+// The raw words of entries e0 .. e0+15 (e0 a multiple of 16): two 16-byte
+// loads through L2, where a row just streamed still is, when the entries
+// are whole and aligned; else 16 loads, with 0xFFFF (key 0) past the row end.
+__device__ __forceinline__ void chunk_raw(const KParams& P, int row, int e0, uint4& a, uint4& b) {
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + e0;
+  if (P.vec_ok && e0 + kEPT <= P.V) {
+    const uint4* g = reinterpret_cast<const uint4*>(src);
+    a = __ldcg(g);
+    b = __ldcg(g + 1);
+  } else {
+    uint32_t wv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t lo = (e0 + 2 * j < P.V) ? static_cast<uint32_t>(src[2 * j]) : 0xFFFFu;
+      const uint32_t hi = (e0 + 2 * j + 1 < P.V) ? static_cast<uint32_t>(src[2 * j + 1]) : 0xFFFFu;
+      wv[j] = lo | (hi << 16);
+    }
+    a = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    b = make_uint4(wv[4], wv[5], wv[6], wv[7]);
   }
 }
 
@@ -905,14 +936,23 @@ __device__ __forceinline__ float emass(float y, float T, float rT, float q, bool
   return t1 ? ex2_approx(__fmul_rn(__fsub_rn(y, q), kLog2e)) : mass_of(y, T, rT, q);
 }
 
+// Reference of a segment whose sum is already relative to the row max M
+// (masses from mass_of): rescaling by 2^(RN(M log2e) - M log2e) would scale
+// it by the rounding error of M log2e, which for large M (small T) is not
+// negligible.
+constexpr float kRelM = INFINITY;
+
 // segment s's mass rescaled to M: ss 2^(c - M log2e), with the exponent
 // rounded once (0 past nseg, for empty segments and for references far
-// enough below M to underflow; NaN sums stay NaN)
+// enough below M to underflow; NaN sums stay NaN; sums with reference kRelM
+// as they are)
 __device__ __forceinline__ float seg_mass(const RSmem& S, int s, int nseg, float M) {
   if (s >= nseg) return 0.f;
   const float ss = S.ss[s];
   if (ss != ss) return ss;
-  return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmaf_rn(-M, kLog2e, S.sq[s]))) : 0.f;
+  const float q = S.sq[s];
+  if (q == kRelM) return ss;
+  return (ss > 0.f) ? __fmul_rn(ss, ex2_approx(__fmaf_rn(-M, kLog2e, q))) : 0.f;
 }
 
 // ------------------------------------------------------------ selection over the finish
@@ -964,6 +1004,233 @@ __device__ uint32_t radix_kth(const KParams& P, RSmem& S, int row, int R, unsign
   unsigned ab2;
   const int lb = h256_select_desc(S, k - above, &ab2);
   return (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(lb);
+}
+
+// ------------------------------------------------ rows finished from chunk records
+// Unsplit top-k rows keep no candidates while streaming.  Instead, for every
+// chunk of 16 entries (round r, thread t: entries r kRound + 16 t .. + 15,
+// chunk index c = r kT + t) the stream records the chunk's top key, in the
+// ckey and cidx regions (kRecRounds rounds at most).
+constexpr int kRecRounds = kCB * (sizeof(uint16_t) + sizeof(uint32_t)) / sizeof(uint16_t) / kT;   // 24
+static_assert(offsetof(RSmem, cidx) == offsetof(RSmem, ckey) + sizeof(RSmem::ckey), "records span ckey and cidx");
+__device__ __forceinline__ uint16_t* recs(RSmem& S) { return S.ckey; }
+
+// raw word j (0..15) of a chunk held as two uint4
+__device__ __forceinline__ uint32_t raw_at(const uint4& a, const uint4& b, int j) {
+  const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t w = wv[0];
+#pragma unroll
+  for (int q = 1; q < 8; ++q)
+    if ((j >> 1) == q) w = wv[q];
+  return (j & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+struct LeanRes {
+  bool ok;                     // false: nothing decided, the caller takes the re-streaming paths
+  int result;
+  float Z;
+  uint32_t key_lo_k, key_lo, kdraw;
+};
+
+// The repetition-penalty patch of a chunk's 16 raw words (two uint4), as the
+// stream applied it.
+template <int DT>
+__device__ __forceinline__ void patch_chunk(const KParams& P, const RSmem& S, int row, int e0, uint4& a, uint4& b) {
+  uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float yv[kEPT];
+#pragma unroll
+  for (int j = 0; j < kEPT; ++j) yv[j] = DType<DT>::to_f32((j & 1) ? (wv[j >> 1] >> 16) : (wv[j >> 1] & 0xFFFFu));
+  patch16<DT>(P, S, row, e0, yv);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t lo = (e0 + 2 * j < P.V) ? DType<DT>::to_raw(yv[2 * j]) : 0xFFFFu;
+    const uint32_t hi = (e0 + 2 * j + 1 < P.V) ? DType<DT>::to_raw(yv[2 * j + 1]) : 0xFFFFu;
+    wv[j] = lo | (hi << 16);
+  }
+  a = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  b = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+}
+
+// bit j set where key j of the chunk is >= f (f >= 1: key 0, past the row
+// end, never is)
+__device__ __forceinline__ uint32_t chunk_mask(const uint4& a, const uint4& b, uint32_t f) {
+  const uint32_t fm2 = (f - 1u) * 0x00010001u;
+  const uint32_t wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t m = 0u;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t s2 = surv2(keys2(wv[q]), fm2);   // 1 in each half whose key >= f
+    m |= ((s2 & 1u) | ((s2 >> 15) & 2u)) << (2 * q);
+  }
+  return m;
+}
+
+// Flagged chunks: a list in vocab order (in S.lp); item i's 16 entries, with
+// the penalty patch applied, are cached in the stages from kLeanCacheOff on.
+constexpr int kLeanCacheOff = kHB * 4 / 16;                       // uint4 index: after the counts
+constexpr int kLeanCacheCap = (kStages * kRVecs - kLeanCacheOff) / 2;   // chunks (3584)
+
+// Thresholds and draw of a record row.
+//   1. A floor F that every kept entry reaches: the k-th largest of the
+//      threads' largest records (k chunks hold an entry at or above it, so
+//      the row's k-th largest key is not below it, and top-p acts on the
+//      top-k set).  When the records do not place F within the 4096 keys
+//      under the row max, F is the lowest key of that window.  Every entry
+//      at or above F lies in a chunk whose top key is at or above F.
+//   2. Those chunks, listed in vocab order and spread evenly over the
+//      threads, are re-read (from L2) once and cached in shared memory; their
+//      entries at or above F are counted per key: tau_k and tau_p as on the
+//      candidate path.
+//   3. Thread t holds list items [q t, q t + q), so thread order is vocab
+//      order: per-thread kept masses, one block scan, and the thread holding
+//      u Z walks its items to the drawn entry.
+// Returns ok = false when a threshold falls below F (the window), the list
+// outgrows the cache, or no kept entry has mass.
+template <int DT>
+__device__ __forceinline__ LeanRes lean_finish(const KParams& P, RSmem& S, int row, int R, uint32_t kmax, float M, float T,
+                                            float rT, int k, bool topp, float pp, uint32_t key_cut, float u, int& ph) {
+  using C = Codec<DT, 16>;
+  const int tid = threadIdx.x;
+  LeanRes res{false, 0, 0.f, 0u, 0u, 0u};
+  const uint16_t* rec1 = recs(S);
+  unsigned* cnt = reinterpret_cast<unsigned*>(&S.stage[0][0]);   // exact counts, bin b: key kmax - b
+  unsigned* cf = cnt + kHB;                                       // counts of recorded keys (the floor)
+  uint4* cache = &S.stage[0][0] + kLeanCacheOff;                  // overlaps cf: used after the floor
+  uint16_t* list = reinterpret_cast<uint16_t*>(S.lp);
+  const uint32_t klo = (kmax >= static_cast<uint32_t>(kHB)) ? kmax - static_cast<uint32_t>(kHB - 1) : 1u;
+  for (int i = tid; i < kHB; i += kT) { cnt[i] = 0u; cf[i] = 0u; }
+  __syncthreads();
+
+  // ---- 1. the floor, from counts of the threads' largest records
+  uint32_t km = 0u;
+  for (int r = 0; r < R; ++r) km = max(km, static_cast<uint32_t>(rec1[r * kT + tid]));
+  if (km >= klo) atomicAdd(&cf[kmax - km], 1u);
+  __syncthreads();
+  int ftot;
+  const unsigned fb = cnth_select(cf, k, S, ph, &ftot);
+  const uint32_t F = (ftot < k || fb == static_cast<unsigned>(INT_MAX)) ? klo : kmax - fb;
+
+  // ---- 2. the flagged chunks in vocab order, read once
+  const int nch = (P.V + kEPT - 1) / kEPT;
+  const int c0 = tid * R, c1 = min(c0 + R, nch);
+  int nf = 0;
+  for (int c = c0; c < c1; ++c) nf += rec1[c] >= F ? 1 : 0;
+  int n;
+  int o = rscan_i(nf, S, ph, &n);
+  if (n > kLeanCacheCap) return res;
+  for (int c = c0; c < c1; ++c)
+    if (rec1[c] >= F) list[o++] = static_cast<uint16_t>(c);
+  __syncthreads();
+  const int q = (n + kT - 1) / kT;
+  const int i0 = min(tid * q, n), i1 = min(i0 + q, n);
+  const bool pen = row_has_penalty(P, row);
+  {
+    // one chunk in flight while the previous one is counted
+    uint4 na = make_uint4(0u, 0u, 0u, 0u), nb = na;
+    if (i0 < i1) chunk_raw(P, row, static_cast<int>(list[i0]) * kEPT, na, nb);
+    for (int i = i0; i < i1; ++i) {
+      uint4 ca = na, cb = nb;
+      if (i + 1 < i1) chunk_raw(P, row, static_cast<int>(list[i + 1]) * kEPT, na, nb);
+      if (pen) patch_chunk<DT>(P, S, row, static_cast<int>(list[i]) * kEPT, ca, cb);
+      for (uint32_t m = chunk_mask(ca, cb, F); m; m &= m - 1u)
+        atomicAdd(&cnt[kmax - key16(raw_at(ca, cb, __ffs(m) - 1))], 1u);
+      cache[2 * i] = ca;
+      cache[2 * i + 1] = cb;
+    }
+  }
+  __syncthreads();
+
+  // ---- thresholds, as on the candidate path
+  int ktot;
+  const unsigned ksel = cnth_select(cnt, k, S, ph, &ktot);
+  if (ktot < k || ksel == static_cast<unsigned>(INT_MAX)) return res;
+  const uint32_t key_lo_k = tie_floor<DT, 16>(kmax - ksel, T);
+  if (key_lo_k < F) return res;
+  uint32_t key_lo = key_lo_k;
+  if (topp) {
+    const int bk = static_cast<int>(kmax - key_lo_k);
+    float m4[4];
+    float s4 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = tid * 4 + j;
+      const unsigned cn = cnt[b];
+      m4[j] = (b <= bk && cn) ? __fmul_rn(static_cast<float>(cn), mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M)) : 0.f;
+      s4 += m4[j];
+    }
+    float tot;
+    const float ex = rscan_f(s4, S, ph, &tot);
+    const float target = __fmul_rn(pp, tot);   // top-p over the top-k set
+    int mine = INT_MAX;
+    if (s4 > 0.f && ex + s4 >= target) {
+      float acc = ex;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (mine == INT_MAX && m4[j] > 0.f && acc + m4[j] >= target) mine = tid * 4 + j;
+        acc += m4[j];
+      }
+      if (mine == INT_MAX) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (m4[j] > 0.f) mine = tid * 4 + j;
+      }
+    }
+    unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+    const bool reached = tot >= target;
+    if (bsel == static_cast<unsigned>(INT_MAX) && reached) {
+      int last = -1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (m4[j] > 0.f) last = tid * 4 + j;
+      bsel = static_cast<unsigned>(static_cast<int>(rmax_u(static_cast<unsigned>(last + 1), S, ph)) - 1);
+    }
+    if (!reached || bsel == static_cast<unsigned>(INT_MAX) || bsel == 0xFFFFFFFFu) return res;
+    key_lo = max(tie_floor<DT, 16>(kmax - bsel, T), key_lo_k);
+    if (key_lo < F) return res;
+  }
+  const uint32_t kdraw = max(key_lo, key_cut);
+
+  // ---- 3. the draw: kept masses per thread in vocab order
+  float wsum = 0.f;
+  for (int i = i0; i < i1; ++i) {
+    const uint4 ca = cache[2 * i], cb = cache[2 * i + 1];
+    for (uint32_t m = chunk_mask(ca, cb, kdraw); m; m &= m - 1u)
+      wsum += mass_of(DType<DT>::to_f32(raw_at(ca, cb, __ffs(m) - 1)), T, rT, M);
+  }
+  float Z;
+  const float ex = rscan_f(wsum, S, ph, &Z);
+  const float target = __fmul_rn(u, Z);
+  const unsigned mine = (wsum > 0.f && ex + wsum > target) ? static_cast<unsigned>(tid) : static_cast<unsigned>(INT_MAX);
+  unsigned pick, lastp;
+  rminmax_u(mine, wsum > 0.f ? static_cast<unsigned>(tid + 1) : 0u, S, ph, &pick, &lastp);
+  if (pick == static_cast<unsigned>(INT_MAX) && lastp == 0u) return res;
+  const bool take_last = pick == static_cast<unsigned>(INT_MAX);
+  const int owner = take_last ? static_cast<int>(lastp) - 1 : static_cast<int>(pick);
+  if (tid == owner) {
+    // the same sums in the same order: ex + (running sum) crosses the target
+    // inside this thread's items, or the last kept entry is taken
+    float run = 0.f;
+    int hit = -1, lastk = -1;
+    for (int i = i0; i < i1 && hit < 0; ++i) {
+      const uint4 ca = cache[2 * i], cb = cache[2 * i + 1];
+      const int e0 = static_cast<int>(list[i]) * kEPT;
+      for (uint32_t m = chunk_mask(ca, cb, kdraw); m && hit < 0; m &= m - 1u) {
+        const int j = __ffs(m) - 1;
+        run += mass_of(DType<DT>::to_f32(raw_at(ca, cb, j)), T, rT, M);
+        lastk = e0 + j;
+        if (!take_last && ex + run > target) hit = e0 + j;
+      }
+    }
+    S.ib[4] = hit >= 0 ? hit : lastk;
+  }
+  __syncthreads();
+  res.ok = S.ib[4] >= 0;
+  res.result = S.ib[4];
+  res.Z = Z;
+  res.key_lo_k = key_lo_k;
+  res.key_lo = key_lo;
+  res.kdraw = kdraw;
+  return res;
 }
 
 // ------------------------------------------------ dense top-p rows
@@ -1024,7 +1291,6 @@ __device__ bool dense_topp(const KParams& P, RSmem& S, int row, int R, uint32_t 
   // pass 2: masses above hi per segment, bracket entries into the regions
   int fill = 0;
   bool ovf = false;
-  const float Mq = __fmul_rn(M, kLog2e);
   stream_row<DT>(P, S, row, 0, R, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
     float e[kEPT];
     masses16<DT>(raw, T, rT, M, e);
@@ -1039,7 +1305,7 @@ __device__ bool dense_topp(const KParams& P, RSmem& S, int row, int R, uint32_t 
       }
     }
     a = warp_sum(a);
-    if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = Mq; }
+    if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = kRelM; }
     const int c = __popc(sb);
     int incl = c;
 #pragma unroll
@@ -1304,6 +1570,9 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     }
     const bool mass_all = !VPL && sampled && !topk;   // S over the whole row
     const bool segs = mass_all && !topp;              // draw from segment sums
+    // unsplit top-k rows record chunk top keys instead of keeping
+    // candidates (lean_finish)
+    const bool lean = !SPLIT && !VPL && N > 0 && topk && R <= kRecRounds;
 
     // running state
     unsigned best = 0u;       // thread max key
@@ -1316,15 +1585,21 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     uint32_t kcut = 0u;       // mass rows: warps whose keys all lie below skip their masses
     const uint32_t kinf = C::from_val(INFINITY), kninf = C::from_val(-INFINITY);
 
-    stream_row<DT>(P, S, row, r0, r1, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+    // The round body, specialised per row mode at compile time (bit 0:
+    // masses over the whole row; bit 1: per-segment masses; bit 2:
+    // candidates), so each mode's stream loop carries only its own work.
+    auto round_body = [&](auto mode, int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
+      constexpr int MD = decltype(mode)::value;
+      constexpr bool kMass = (MD & 1) != 0, kSegs = (MD & 2) != 0, kCand = (MD & 4) != 0, kRec = (MD & 8) != 0;
       const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
                                   max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
-      const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);  // padding keys are 0
+      const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);   // padding keys are 0
+      if constexpr (kRec) recs(S)[(r - r0) * kT + tid] = static_cast<uint16_t>(tm);
       if (tm > best) { best = tm; bround = r; }
       uint32_t k0 = 0u;  // max of the part's first round (that round only)
-      if (r == r0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
+      if ((kMass || kCand) && r == r0 && (mass_all || !overflow)) k0 = rmax_u(tm, S, ph);
 
-      if (mass_all) {
+      if constexpr (kMass) {
         if (r == r0) {
           // entries with y below y0 - 36 T have mass below e^-36 relative to
           // the row max; all of them together stay below V e^-36 < 1e-9 of S
@@ -1359,6 +1634,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
         if (lane == 0) { S.ss[r * kNW + warp] = ws; S.sq[r * kNW + warp] = cq; }
       }
 
+      if constexpr (kCand) {
       if (!overflow) {
         if (r == r0) {
           // First floor: the N0-th largest of the threads' round-0 maxima,
@@ -1390,16 +1666,20 @@ __device__ __forceinline__ void row_body(const KParams& P) {
           for (int q = 0; q < 8; ++q) sb |= surv2(w[q], fm2) << q;
           return sb;
         };
-        // warp-level exclusive prefix of the lanes' survivor counts
+        // warp-level exclusive prefix of the lanes' survivor counts: one
+        // ballot when no lane holds more than one, else a shuffle scan
         auto lane_scan = [&](uint32_t bits, int* tot) -> int {
           const int c = __popc(bits);
+          const unsigned nz = __ballot_sync(0xFFFFFFFFu, c != 0);
+          if (!__any_sync(0xFFFFFFFFu, c > 1)) {
+            *tot = __popc(nz);
+            return __popc(nz & ((1u << lane) - 1u));
+          }
           int incl = c;
-          if (__any_sync(0xFFFFFFFFu, c != 0)) {
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-              if (lane >= o) incl += y;
-            }
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += y;
           }
           *tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
           return incl - c;
@@ -1441,10 +1721,24 @@ __device__ __forceinline__ void row_body(const KParams& P) {
           fill += total;
         }
       }
-    });
+      }
+    };
+    using std::integral_constant;
+    const int smode = lean ? 8 : ((mass_all ? 1 : 0) | (segs ? 2 : 0) | (!overflow ? 4 : 0));
+#define ECAH_ROUND(M) stream_row<DT>(P, S, row, r0, r1, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) { round_body(integral_constant<int, M>{}, r, st, raw, w, nv); })
+    switch (smode) {
+      case 0: ECAH_ROUND(0); break;
+      case 1: ECAH_ROUND(1); break;
+      case 3: ECAH_ROUND(3); break;
+      case 4: ECAH_ROUND(4); break;
+      case 5: ECAH_ROUND(5); break;
+      case 8: ECAH_ROUND(8); break;
+      default: ECAH_ROUND(7); break;   // no row mode sets other bits together
+    }
+#undef ECAH_ROUND
 
     unsigned* cnth = reinterpret_cast<unsigned*>(&S.stage[0][0]) + kCntOff;  // [kHB] counts, bin b = key kmax - b
-    if (N > 0) {
+    if (N > 0 && !lean) {
       // the warps' floors and regions -> one floor F (their max) and one
       // buffer in vocab order holding every entry of the row with key >= F
       overflow = __syncthreads_or(overflow) != 0;
@@ -1453,7 +1747,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
         fill = gather_candidates(S, fill, ph);
       }
     }
-    bool cand = N > 0 && !overflow;   // every entry with key >= f is in the buffer
+    bool cand = N > 0 && !overflow && !lean;   // every entry with key >= f is in the buffer
 
     // ------------------------------------------------ row max and greedy
     unsigned kmax, fmax;
@@ -1545,6 +1839,23 @@ __device__ __forceinline__ void row_body(const KParams& P) {
         mass_ok = isfinite(S_all);
       }
       bool fast = (!overflow || segs) && mass_ok;
+      // record rows: floor, thresholds and draw from the chunk records; when
+      // they decide nothing, the re-streaming paths below take the row
+      bool lean_done = false;
+      float lean_Z = 0.f;
+      int lean_result = 0;
+      if (lean) {
+        const LeanRes lr = lean_finish<DT>(P, S, row, R, kmax, M, T, rT, k_eff, topp, pp, key_cut, u, ph);
+        if (lr.ok) {
+          lean_done = true;
+          key_lo_k = lr.key_lo_k;
+          key_lo = lr.key_lo;
+          lean_Z = lr.Z;
+          lean_result = lr.result;
+        } else {
+          fast = false;   // the re-streaming paths below
+        }
+      }
       if (thr) {
         const int Bmax = static_cast<int>(kmax - F);
         // top-k: the k-th largest key among the candidates
@@ -1691,7 +2002,10 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       const uint32_t kdraw = max(key_lo, key_cut);
       float Z = 0.f;
       bool none = false;
-      if (fast && (topk || topp)) {
+      if (lean_done) {
+        Z = lean_Z;
+        result = lean_result;
+      } else if (fast && (topk || topp)) {
         // inverse CDF over the candidates, in vocab order (entries 8*tid .. 8*tid+7)
         float e[8];
         float s8 = 0.f;
@@ -1735,7 +2049,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
               if (j < nv && key >= kdraw) a += mass_of(C::value(key), T, rT, M);
             }
             a = warp_sum(a);
-            if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = __fmul_rn(M, kLog2e); }
+            if (lane == 0) { S.ss[r * kNW + warp] = a; S.sq[r * kNW + warp] = kRelM; }
           });
         }
         // per-segment mass relative to M, then the segment holding u * Z
