@@ -13,7 +13,7 @@ from ctypes import c_int32, c_int64, c_size_t, c_uint32, c_void_p
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "lib", "libecah_sampler.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 FLAG_FREQ_PRES = 0x1
 
@@ -41,6 +41,7 @@ class SamplerArgs(ctypes.Structure):
         ("flags", c_uint32),
         ("uniforms", c_void_p), ("philox_state", c_void_p), ("out", c_void_p), ("row_stats", c_void_p), ("probs_out", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("row_index", c_void_p), ("logit_rows", c_int32),
     ]
 
 

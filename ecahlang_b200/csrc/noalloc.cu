@@ -12,15 +12,16 @@
 //
 // The scratch is a file-scope __device__ array of kNoAllocScratchBytes; every
 // GPU that loads the library holds it until the process exits.  Its device
-// address is looked up once per device, on the first call made with that
-// device current (cudaGetSymbolAddress); make that first call outside any
-// stream capture.  Every call shares the array: it is cleared on the caller's
-// stream before each launch, and calls whose work overlaps on the GPU (two
-// streams at once) race on it.
+// address is looked up on every call, with the calling device current
+// (cudaGetSymbolAddress, which allocates nothing), so it stays right after a
+// cudaDeviceReset; the first call on a device may load the module, so make it
+// outside any stream capture.  Every call shares the array: it is cleared on
+// the caller's stream before each launch, and calls whose work overlaps on
+// the GPU (two streams at once) race on it.  The scratch holds what the
+// cluster kernel needs, so every launch through this entry point runs the
+// cluster kernel.
 
 #include <cuda_runtime.h>
-
-#include <mutex>
 
 #include "../../include/ecah_sampler.h"
 
@@ -30,28 +31,17 @@ extern "C" size_t ecah_internal_min_workspace_bytes(void);
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 256;
-constexpr int kMaxDevices = 64;
-
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array for the current device (host code sees
+// Device address of the scratch array on the current device (host code sees
 // only a host-side stand-in for the symbol, never usable as a device pointer).
 void* scratch_for_current_device() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    g_scratch_ptr[dev] = p;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
   }
-  return g_scratch_ptr[dev];
+  return p;
 }
 
 }  // namespace

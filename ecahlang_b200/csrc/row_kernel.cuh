@@ -214,7 +214,7 @@ __device__ void complete_slice(const KParams& P, const RSmem& S, uint4* st, int 
   const int lane = threadIdx.x & 31;
   const int n = slice_len(P.V, r);
   const int e0 = slice_e0(r);
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + e0;
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + e0;
   uint16_t* raw = reinterpret_cast<uint16_t*>(st);
   const int done = P.vec_ok ? ((n >> 3) << 3) : 0;
   if (done < kWS) {
@@ -370,7 +370,7 @@ __device__ void patch16(const KParams& P, const RSmem& S, int row, int e0, float
 // repetition-penalty patch applied (NaN past the row end)
 template <int DT>
 __device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride;
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row);
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
   patch16<DT>(P, S, row, e0, yv);
@@ -380,7 +380,7 @@ __device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float 
 // loads through L2, where a row just streamed still is, when the entries
 // are whole and aligned; else 16 loads, with 0xFFFF (key 0) past the row end.
 __device__ __forceinline__ void chunk_raw(const KParams& P, int row, int e0, uint4& a, uint4& b) {
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + e0;
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + e0;
   if (P.vec_ok && e0 + kEPT <= P.V) {
     const uint4* g = reinterpret_cast<const uint4*>(src);
     a = __ldcg(g);
@@ -416,7 +416,7 @@ __device__ void stream_row(const KParams& P, RSmem& S, int row, int r0, int r1, 
   // this thread's chunks: the warp's slice of round r starts at chunk
   // r * kRVecs + warp * kWV; lane l copies chunks l and l + 32 of it
   const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
-                                                    static_cast<long long>(row) * P.row_stride) +
+                                                    logits_row_offset(P, row)) +
                      warp * kWV + lane;
   uint4* wst = &S.stage[0][0] + warp * (kStages * kWV);   // this warp's stages
   const int last_nv = max(0, min(kEPT, round_len(P.V, R - 1) - kEPT * static_cast<int>(threadIdx.x)));
@@ -1590,7 +1590,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     // candidates), so each mode's stream loop carries only its own work.
     auto round_body = [&](auto mode, int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
       constexpr int MD = decltype(mode)::value;
-      constexpr bool kMass = (MD & 1) != 0, kSegs = (MD & 2) != 0, kCand = (MD & 4) != 0, kRec = (MD & 8) != 0;
+      constexpr bool kMass = (MD & 1) != 0, kCand = (MD & 4) != 0, kRec = (MD & 8) != 0;   // bit 1: segment masses (the same code)
       const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
                                   max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
       const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);   // padding keys are 0

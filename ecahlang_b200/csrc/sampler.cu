@@ -1,11 +1,13 @@
 // Host launcher and small kernels of libecah_sampler.so (C ABI in
-// include/ecah_sampler.h).  The sampler kernels are in stream_kernel.cuh (16-bit
-// keys: fp16/bf16 logits without additive penalties, given the full workspace)
-// and sampler_kernel.cuh (everything else).
+// include/ecah_sampler.h).  The sampler kernels are the row kernel
+// (row_kernel.cuh: fp16/bf16 logits without additive penalties, given the
+// full workspace) and the cluster kernel (sampler_kernel.cuh: everything
+// else); stream_kernel.cuh writes probs_out after the row kernel.
 
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "row_kernel.cuh"
 #include "vp_kernel.cuh"
@@ -198,6 +200,41 @@ const char* ecah_status_string(int s) {
   }
 }
 
+// cudaFuncSetAttribute once per (kernel, device, value): the attribute is a
+// property of the kernel on a device, so later launches skip the call.
+// forget_smem drops the remembered values (a launch that failed sets them
+// again: after cudaDeviceReset the kernels come back without them).
+static std::mutex g_smem_mu;
+static constexpr int kSmemSlots = 64;
+static KernelFn g_smem_fn[kSmemSlots];
+static int g_smem_dev[kSmemSlots], g_smem_val[kSmemSlots];
+static int g_smem_used = 0;
+
+static void forget_smem() {
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  g_smem_used = 0;
+}
+
+static cudaError_t set_smem_once(KernelFn fn, int smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  KernelFn* fns = g_smem_fn;
+  int* devs = g_smem_dev;
+  int* vals = g_smem_val;
+  int& used = g_smem_used;
+  constexpr int kSlots = kSmemSlots;
+  for (int i = 0; i < used; ++i)
+    if (fns[i] == fn && devs[i] == dev && vals[i] >= smem) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  for (int i = 0; i < used; ++i)
+    if (fns[i] == fn && devs[i] == dev) { vals[i] = smem; return cudaSuccess; }
+  if (used < kSlots) { fns[used] = fn; devs[used] = dev; vals[used] = smem; ++used; }
+  return cudaSuccess;
+}
+
 size_t ecah_sampler_workspace_bytes(int32_t batch, int32_t vocab, int32_t dtype) {
   RowLayout L;
   if (!k16_dtype(dtype) || !row_layout(batch, vocab, &L)) return kMinWorkspace;
@@ -222,10 +259,13 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   if (!a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
   if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
   if (!a->workspace || a->workspace_bytes < kMinWorkspace) return ECAH_ERR_WORKSPACE;
+  if (a->row_index && a->logit_rows < 1) return ECAH_ERR_SHAPE;
 
   KParams P = {};
   P.logits = a->logits;
   P.row_stride = a->row_stride;
+  P.row_index = a->row_index;
+  P.logit_rows = a->row_index ? a->logit_rows : a->batch;
   P.B = a->batch;
   P.V = a->vocab;
   P.temperature = a->temperature;
@@ -276,9 +316,15 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
       fn = L.parts > 1 ? rk::row_sample_kernel<ECAH_DTYPE_F16, true> : rk::row_sample_kernel<ECAH_DTYPE_F16, false>;
     else
       fn = L.parts > 1 ? rk::row_sample_kernel<ECAH_DTYPE_BF16, true> : rk::row_sample_kernel<ECAH_DTYPE_BF16, false>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (set_smem_once(fn, smem) != cudaSuccess)
       return ECAH_ERR_LAUNCH;
     fn<<<grid, rk::kT, smem, s>>>(P);
+    if (cudaPeekAtLastError() != cudaSuccess) {
+      cudaGetLastError();
+      forget_smem();
+      if (set_smem_once(fn, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
+      fn<<<grid, rk::kT, smem, s>>>(P);
+    }
     if (a->probs_out) {
       if (a->dtype == ECAH_DTYPE_F16) stream_probs_kernel<ECAH_DTYPE_F16><<<all, kThreads, 0, s>>>(P);
       else stream_probs_kernel<ECAH_DTYPE_BF16><<<all, kThreads, 0, s>>>(P);
@@ -296,7 +342,7 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   P.fx_inv = ldexpf(1.0f, -plan.fx_log2);
 
   KernelFn fn = pick_kernel(a->dtype, plan.kb);
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem));
+  cudaError_t e = set_smem_once(fn, static_cast<int>(plan.smem));
   if (e != cudaSuccess) return ECAH_ERR_LAUNCH;
   if (plan.CL > 8) {
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -371,7 +417,7 @@ int ecah_vp_local(const ecah_vp_args* a, void* stream) {
   if (sms <= 0) return ECAH_ERR_LAUNCH;
   const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
   KernelFn fn = a->dtype == ECAH_DTYPE_F16 ? rk::vp_local_row_kernel<ECAH_DTYPE_F16> : rk::vp_local_row_kernel<ECAH_DTYPE_BF16>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
+  if (set_smem_once(fn, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
   fn<<<grid, rk::kT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
   return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
@@ -424,7 +470,7 @@ int ecah_vp_step(const ecah_vp_args* a, const ecah_vp_peers* x, void* stream) {
   if (sms <= 0) return ECAH_ERR_LAUNCH;
   const dim3 grid(static_cast<unsigned>(a->batch < sms ? a->batch : sms));
   KernelFn fn = a->dtype == ECAH_DTYPE_F16 ? rk::vp_step_row_kernel<ECAH_DTYPE_F16> : rk::vp_step_row_kernel<ECAH_DTYPE_BF16>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
+  if (set_smem_once(fn, smem) != cudaSuccess) return ECAH_ERR_LAUNCH;
   fn<<<grid, rk::kT, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
   return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }

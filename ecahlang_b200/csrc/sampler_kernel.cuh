@@ -48,6 +48,8 @@ namespace cg = cooperative_groups;
 struct KParams {
   const void* logits;
   long long row_stride;
+  const int* row_index;    // [B] logits row of each row (NULL: row r)
+  int logit_rows;          // rows of the logits buffer (with row_index)
   int B, V;
   const float* temperature;
   const int* top_k;
@@ -97,6 +99,14 @@ struct KParams {
   long long vp_lflag, vp_lcount, vp_lcand;   // region offsets in an exchange buffer
   unsigned long long vp_timeout_ns; // per wait on another rank's flag
 };
+
+// Element offset of row `row`'s logits: row_index[row] (clamped into
+// [0, logit_rows)) rows in when the launch gathers rows, else `row` rows.
+__device__ __forceinline__ long long logits_row_offset(const KParams& P, int row) {
+  long long r = row;
+  if (P.row_index) r = min(max(P.row_index[row], 0), P.logit_rows - 1);
+  return r * P.row_stride;
+}
 
 constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private
 constexpr int kNBL = 512;     // bins of deeper levels / the key window
@@ -402,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
   const int c0 = rank * P.CH;
   const int n = max(0, min(P.CH, P.V - c0));
   const int nvec = (n + N - 1) / N;
-  const Raw* src = reinterpret_cast<const Raw*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
+  const Raw* src = reinterpret_cast<const Raw*>(P.logits) + logits_row_offset(P, row) + c0;
 
   for (int i = tid; i < kWin; i += kThreads) S.win[i] = 0u;
   for (int i = tid; i < kNBL; i += kThreads) S.c3[i] = 0u;

@@ -94,7 +94,7 @@ __device__ void warp_select_seq(const T* hist, T target, int* out_bin, T* out_ab
 __device__ __forceinline__ void issue_chunk(const KParams& P, uint4* buf, int row, int c, int n) {
   if (!P.vec_ok) return;
   const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) +
-                                                   static_cast<long long>(row) * P.row_stride + c * kSCH);
+                                                   logits_row_offset(P, row) + c * kSCH);
   const int nfull = n >> 3;
   for (int v = threadIdx.x; v < nfull; v += kThreads) cp_async16(buf + v, s4 + v);
 }
@@ -104,7 +104,7 @@ __device__ void complete_chunk(const KParams& P, uint4* buf, int row, int c, int
   using Dt = DType<DT>;
   const int tid = threadIdx.x;
   const int c0 = c * kSCH;
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + static_cast<long long>(row) * P.row_stride + c0;
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + c0;
   uint16_t* raw = reinterpret_cast<uint16_t*>(buf);
   const int done = P.vec_ok ? ((n >> 3) << 3) : 0;
   for (int i = done + tid; i < kSCH; i += kThreads) raw[i] = (i < n) ? src[i] : static_cast<uint16_t>(0xFFFFu);

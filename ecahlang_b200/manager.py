@@ -202,12 +202,27 @@ class SamplingManager:
                 self.sampling_slot_gpu[:B], self.sampling_out[:B], self._fp_eager)
 
     def sample(self, logits: torch.Tensor, bucket_size: Optional[int] = None,
-               uniforms: Optional[torch.Tensor] = None) -> torch.Tensor:
+               uniforms: Optional[torch.Tensor] = None, row_index=None) -> torch.Tensor:
         """One token per row of ``logits`` [B, V] (B = bucket_size for the
         CUDA-graph buffers, else the filled rows), penalties from the rows'
         slots.  Enqueued on the current stream; capturable into a CUDA graph
-        (the Philox offset advances on the device)."""
-        B = logits.shape[0]
+        (the Philox offset advances on the device).
+
+        ``row_index`` samples rows of a larger [L, V] buffer instead: the
+        prefill's ``output.logits[0]`` with the last token of each request,
+        ``append_indptr[1:] - 1`` (ecahlang/main.py:476), read in place.  A
+        host sequence is range-checked here and copied to the device; a
+        device int32 tensor is used as it is."""
+        if row_index is not None:
+            if not torch.is_tensor(row_index) or not row_index.is_cuda:
+                idx = np.asarray(torch.as_tensor(row_index).cpu() if torch.is_tensor(row_index) else row_index,
+                                 dtype=np.int64).reshape(-1)
+                if idx.size and (idx.min() < 0 or idx.max() >= logits.shape[0]):
+                    raise IndexError(f"row_index outside [0, {logits.shape[0]})")
+                row_index = torch.as_tensor(idx.astype(np.int32)).to(self.device, non_blocking=True)
+            B = row_index.numel()
+        else:
+            B = logits.shape[0]
         if bucket_size is not None and B != bucket_size:
             raise RuntimeError(f"bucket {bucket_size} needs {bucket_size} logits rows, got {B}")
         T, K, P, rep, freq, pres, slot, out, fp = self._buffers(B, bucket_size)
@@ -220,7 +235,32 @@ class SamplingManager:
         return launch(logits, T.view(-1), K, P, out, self._workspace,
                       uniforms=uniforms, philox_state=None if uniforms is not None else self.philox_state,
                       rep_factor=rep, freq_pen=freq if fp else None, pres_pen=pres if fp else None,
-                      penalty=self.penalty, row_slot=slot, freq_pres=fp)
+                      penalty=self.penalty, row_slot=slot, freq_pres=fp, row_index=row_index)
+
+    def sample_async(self, logits: torch.Tensor, bucket_size: Optional[int] = None,
+                     uniforms: Optional[torch.Tensor] = None, row_index=None) -> "PendingIds":
+        """``sample`` plus the device-to-host copy of the ids, without a
+        host sync: the ids go to a pinned host buffer on the current stream
+        and an event marks their arrival.  Replaces ``idx_next.cpu()`` after
+        ``fwd_stream.synchronize()`` (ecahlang/main.py:415-419, :610-615):
+        the host waits on that event only when it needs the ids, and keeps
+        scheduling meanwhile.  Each pending step holds its own pinned buffer,
+        taken from a pool that ``PendingIds.wait`` refills."""
+        ids = self.sample(logits, bucket_size=bucket_size, uniforms=uniforms, row_index=row_index)
+        if not hasattr(self, "_id_pool"):
+            self._id_pool = []
+        n = ids.numel()
+        buf = None
+        for i, b in enumerate(self._id_pool):
+            if b.numel() >= n:
+                buf = self._id_pool.pop(i)
+                break
+        if buf is None:
+            buf = _pinned(torch.empty(max(n, getattr(self, "max_batch_size", n)), dtype=torch.int32))
+        buf[:n].copy_(ids, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        return PendingIds(buf, n, ev, self._id_pool)
 
     def update_penalties(self, ids: torch.Tensor, bucket_size: Optional[int] = None) -> None:
         """Records each row's sampled id in its slot history (rows without a
@@ -230,3 +270,25 @@ class SamplingManager:
         _, _, _, rep, _, _, slot, _, _ = self._buffers(B, bucket_size)
         self.penalty.update(ids.view(-1)[:B], slot[:B], rep[:B])
         self._overflow_host.copy_(self.penalty.overflow, non_blocking=True)
+
+
+class PendingIds:
+    """A step's sampled ids on their way to pinned host memory."""
+
+    def __init__(self, host: torch.Tensor, n: int, event: "torch.cuda.Event", pool: list):
+        self._host, self._n, self._event, self._pool = host, n, event, pool
+        self._ids: Optional[np.ndarray] = None
+
+    def ready(self) -> bool:
+        """True once the ids are on the host (never blocks)."""
+        return self._ids is not None or self._event.query()
+
+    def wait(self) -> np.ndarray:
+        """Blocks on this step's event only, then returns the ids; the pinned
+        buffer goes back to the pool."""
+        if self._ids is None:
+            self._event.synchronize()
+            self._ids = self._host[:self._n].numpy().copy()
+            self._pool.append(self._host)
+            self._host = None
+        return self._ids

@@ -147,12 +147,20 @@ def launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
            freq_pen: Optional[torch.Tensor] = None, pres_pen: Optional[torch.Tensor] = None,
            penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
            freq_pres: bool = False, use_mval: bool = True, row_stats: Optional[torch.Tensor] = None,
-           probs_out: Optional[torch.Tensor] = None, stream: Optional[int] = None) -> torch.Tensor:
+           probs_out: Optional[torch.Tensor] = None, stream: Optional[int] = None,
+           row_index: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Enqueue one sampler launch writing ``out[B]`` (int32).
 
     Optional outputs: ``row_stats`` [B,4] float32 (top-k and final y'
     thresholds, M, Z) and ``probs_out`` [B,V] float32 (the renormalised
-    distribution the draw used)."""
+    distribution the draw used).
+
+    ``row_index`` (int32 [B] on the device) gathers rows: row r samples
+    ``logits[row_index[r]]`` of an [L, V] buffer (the prefill's last token of
+    each request, ``append_indptr[1:] - 1`` in ecahlang/main.py:476) without
+    copying the rows out; parameters, penalty slots and outputs stay indexed
+    by r.  Indices outside [0, L) are clamped on the device, so callers keep
+    them in range (``SamplingManager.sample`` checks host-side indices)."""
     if logits.dim() != 2:
         raise RuntimeError("logits must be [B, V]")
     if logits.dtype not in _DTYPES:
@@ -161,8 +169,12 @@ def launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
         raise RuntimeError("logits must be a CUDA tensor (the sampler has no CPU path)")
     if logits.stride(1) != 1:
         raise RuntimeError("logits rows must be contiguous")
-    B, V = logits.shape
+    L, V = logits.shape
     dev = logits.device
+    B = L
+    if row_index is not None:
+        B = row_index.numel()
+        _need(row_index, "row_index", torch.int32, B, dev)
     _need(temperature, "temperature", torch.float32, B, dev)
     _need(top_k, "top_k", torch.int32, B, dev)
     _need(top_p, "top_p", torch.float32, B, dev)
@@ -181,7 +193,9 @@ def launch(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     a.abi_version = _abi.ABI_VERSION
     a.dtype = _DTYPES[logits.dtype]
     a.batch, a.vocab = B, V
-    a.row_stride = logits.stride(0) if B > 1 else V
+    a.row_stride = logits.stride(0) if L > 1 else V
+    if row_index is not None:
+        a.row_index, a.logit_rows = row_index.data_ptr(), L
     a.logits = logits.data_ptr()
     a.temperature, a.top_k, a.top_p = temperature.data_ptr(), top_k.data_ptr(), top_p.data_ptr()
     a.rep_factor, a.freq_pen, a.pres_pen = _ptr(rep_factor), _ptr(freq_pen), _ptr(pres_pen)

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECAH_SAMPLER_ABI_VERSION 1
+#define ECAH_SAMPLER_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define ECAH_API __attribute__((visibility("default")))
@@ -115,6 +115,14 @@ typedef struct ecah_sampler_args {
                                  Its first 4096 bytes hold counters that every launch
                                  leaves at zero; the rest is scratch.               */
   size_t workspace_bytes;
+  /* Row gather (prefill): row r samples logits row row_index[r] of a
+     [logit_rows, row_stride] buffer, e.g. the last token of each request,
+     append_indptr[1:] - 1 (ecahlang/main.py:476), with no [B, V] copy.
+     NULL = row r reads row r (logit_rows is then ignored).  Entries outside
+     [0, logit_rows) are clamped into it; callers check them.  Penalty slots,
+     parameters and outputs stay indexed by r. */
+  const int32_t* row_index;   /* [B] device                                        */
+  int32_t logit_rows;         /* rows of the logits buffer (>= 1 with row_index)   */
 } ecah_sampler_args;
 
 ECAH_API int ecah_sampler_abi_version(void);
@@ -158,10 +166,13 @@ ECAH_API int ecah_philox_uniforms(uint64_t* philox_state, int32_t batch, float* 
  * counterpart in the reference: FlashInfer's sampler allocates its own state.
  * Scratch is a fixed array of ecah_sampler_noalloc_scratch_bytes() bytes in
  * the library's device memory, held on every GPU that loads the library until
- * exit; shapes whose workspace exceeds it get ECAH_ERR_WORKSPACE.  The first
- * call on a device looks up the array's address (make it outside stream
- * capture); calls share the array, so calls overlapping on the GPU race.
- * args->workspace and args->workspace_bytes are ignored. */
+ * exit.  That is the least any launch accepts, so every shape runs the
+ * cluster kernel (slower than ecah_sampler_launch with a full workspace);
+ * shapes the cluster kernel cannot take get ECAH_ERR_SHAPE.  Every call looks
+ * up the array's address on the current device; the first call on a device
+ * may load the module, so make it outside stream capture.  Calls share the
+ * array, so calls overlapping on the GPU race.  args->workspace and
+ * args->workspace_bytes are ignored. */
 ECAH_API int ecah_sampler_launch_noalloc(const ecah_sampler_args* args, void* stream);
 ECAH_API size_t ecah_sampler_noalloc_scratch_bytes(void);
 

@@ -410,3 +410,47 @@ def test_chi_square_one_million_draws():
     chi2 = float(((c[keep] - exp) ** 2 / exp).sum())
     dof = int(keep.sum()) - 1
     assert chi2 < dof + 6 * np.sqrt(2 * dof), (chi2, dof)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("B", [7, 64])
+def test_row_index_gathers_rows(dtype, B):
+    """The prefill gather (ecahlang/main.py:476, logits[0, append_indptr[1:]-1]):
+    sampling rows row_index[r] of a larger buffer in place gives the same ids,
+    thresholds and masses as sampling the gathered copy, and matches the
+    oracle on those rows; indices past the buffer are clamped, not read."""
+    g = torch.Generator().manual_seed(11 + B)
+    L, V = 150, 32000
+    dev = torch.device("cuda")
+    x = (torch.randn(L, V, generator=g) * 3).to(dtype)
+    idx = torch.randint(0, L, (B,), generator=g, dtype=torch.int32)
+    idx[0], idx[-1] = L - 1, 0
+    T = torch.tensor(np.resize([0.0, 0.7, 1.0, 1.3], B), dtype=torch.float32)
+    K = torch.tensor(np.resize([0, 40, L + V, 5], B), dtype=torch.int32)
+    P = torch.tensor(np.resize([1.0, 0.9, 0.8, 1.0], B), dtype=torch.float32)
+    U = torch.as_tensor(row_uniforms(3, 1, B))
+
+    def run(logits, row_index=None):
+        out = torch.empty(B, dtype=torch.int32, device=dev)
+        stats = torch.zeros(B, 4, dtype=torch.float32, device=dev)
+        ws = S.new_workspace(B, V, dtype, dev)
+        S.launch(logits, T.to(dev), K.to(dev), P.to(dev), out, ws, uniforms=U.to(dev),
+                 row_stats=stats, row_index=row_index)
+        torch.cuda.synchronize()
+        return out.cpu().numpy(), stats.cpu().numpy()
+
+    xd = x.to(dev)
+    got, st = run(xd, idx.to(dev))
+    want, sw = run(x[idx.long()].contiguous().to(dev))
+    assert np.array_equal(got, want)
+    assert np.array_equal(st, sw)
+    xr = x[idx.long()]
+    orc = run_oracle(xr, T.numpy(), K.numpy(), P.numpy(), U.numpy())
+    compare(xr, T.numpy(), K.numpy(), P.numpy(), U.numpy(), (got, st, None), orc)
+    # out-of-range indices are clamped into [0, L)
+    bad = idx.clone()
+    bad[1], bad[2] = -5, L + 9
+    clamped = bad.clamp(0, L - 1)
+    g1, _ = run(xd, bad.to(dev))
+    g2, _ = run(xd, clamped.to(dev))
+    assert np.array_equal(g1, g2)
