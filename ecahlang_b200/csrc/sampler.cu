@@ -14,6 +14,17 @@
 
 namespace ecah {
 
+// ------------------------------------------------------ vocab-parallel reset
+// Exchange-buffer header words: [0] step epoch, [1] rows finished in the
+// step, [2] error (a wait ran out).
+__global__ void vp_reset_kernel(unsigned* hdr, unsigned epoch) {
+  if (threadIdx.x == 0) {
+    hdr[0] = epoch;
+    hdr[1] = 0u;
+    hdr[2] = 0u;
+  }
+}
+
 // ------------------------------------------------------------- hist update
 template <int DT>
 __global__ void hist_update_kernel(const int* ids, int B, const int* row_slot, const float* rep_factor,
@@ -504,6 +515,12 @@ int ecah_vp_ipc_close(void* ptr) {
 int ecah_vp_ipc_free(void* ptr) {
   if (!ptr) return ECAH_ERR_NULL;
   return cudaFree(ptr) == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
+int ecah_vp_reset(void* own_buffer, uint32_t epoch, void* stream) {
+  if (!own_buffer) return ECAH_ERR_NULL;
+  vp_reset_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<unsigned*>(own_buffer), epoch);
+  return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
 
 int ecah_vp_merge(const ecah_vp_args* a, void* stream) {

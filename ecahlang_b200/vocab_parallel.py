@@ -21,7 +21,8 @@ otherwise a callable all-gathers the lists between ``ecah_vp_local`` and
 from __future__ import annotations
 
 import ctypes
-from typing import Callable, Optional
+import time
+from typing import Callable, List, Optional
 
 import torch
 
@@ -51,6 +52,59 @@ def nccl_exchange(group=None) -> Callable[[torch.Tensor, torch.Tensor, torch.Ten
         dist.all_gather_into_tensor(all_cand.view(-1), cand.view(-1), group=group)
         dist.all_gather_into_tensor(all_count.view(-1), count.view(-1), group=group)
     return run
+
+
+class VocabParallelError(RuntimeError):
+    """Rows of a vocab-parallel step came back -1: refused rows (top_k above
+    cand_cap, rows without top-k) or a wait on another rank that ran out."""
+
+
+class RankFailure(RuntimeError):
+    """Another rank did not reach a step within the health check's timeout."""
+
+    def __init__(self, step: int, missing: List[int]):
+        super().__init__(f"ranks {missing} did not reach step {step}")
+        self.step, self.missing = step, missing
+
+
+def agree_epoch(local_epoch: int, all_gather: Callable) -> int:
+    """The step counter every rank resumes from after a failure: the largest
+    over the ranks (a rank that skipped a step lags; flags only grow, so no
+    flag of an earlier step reaches the next step's epoch)."""
+    return max(int(e) for e in all_gather(int(local_epoch)))
+
+
+class RankHealth:
+    """Host-side detection of a rank that raised, hung or left between steps.
+
+    Every rank calls ``before_step(s)`` before launching step s: it records
+    the rank's arrival at s in the store and waits up to ``timeout_s`` for
+    every other rank's, raising ``RankFailure`` with the ranks that did not
+    arrive -- before any kernel or collective of step s is launched, so no
+    rank waits on the device for a peer that is gone.  A rank that fails
+    inside a step (after its arrival) ends the others' collective of that
+    step with an error instead (the process group's timeout bounds it).
+    ``store`` is any torch.distributed Store (TCPStore, FileStore, the
+    default group's store).
+    """
+
+    def __init__(self, store, world: int, rank: int, timeout_s: float = 5.0, prefix: str = "ecah_vp"):
+        self.store, self.world, self.rank, self.timeout_s, self.prefix = store, world, rank, timeout_s, prefix
+
+    def _key(self, rank: int, step: int) -> str:
+        return f"{self.prefix}/step/{rank}/{step}"
+
+    def before_step(self, step: int) -> None:
+        self.store.set(self._key(self.rank, step), "1")
+        deadline = time.monotonic() + self.timeout_s
+        pending = [g for g in range(self.world) if g != self.rank]
+        while pending:
+            pending = [g for g in pending if not self.store.check([self._key(g, step)])]
+            if not pending:
+                return
+            if time.monotonic() > deadline:
+                raise RankFailure(step, pending)
+            time.sleep(0.005)
 
 
 class _DeviceWords:
@@ -97,6 +151,7 @@ class PeerExchange:
         self.own = own.value
         self._mapped = []
         self._barrier = barrier
+        self._all_gather = all_gather
         handles = all_gather(bytes(handle))
         bases = []
         with torch.cuda.device(self.device):
@@ -118,6 +173,25 @@ class PeerExchange:
     def error(self) -> int:
         """Nonzero once a wait on another rank's row ran out (synchronises)."""
         return int(self.header[2].item())
+
+    def epoch(self) -> int:
+        """This rank's step counter (synchronises)."""
+        return int(self.header[0].item()) & 0xFFFFFFFF
+
+    def reset(self) -> int:
+        """Clears the sticky error word and re-syncs the step counter on every
+        rank (collective: every rank calls it, with no step in flight), so
+        the next step waits only for flags of that step.  Returns the epoch
+        the ranks resume from."""
+        torch.cuda.synchronize(self.device)
+        self._barrier()
+        epoch = agree_epoch(self.epoch(), self._all_gather)
+        with torch.cuda.device(self.device):
+            check(lib().ecah_vp_reset(self.own, epoch, torch.cuda.current_stream(self.device).cuda_stream),
+                  "ecah_vp_reset")
+        torch.cuda.synchronize(self.device)
+        self._barrier()
+        return epoch
 
     def close(self) -> None:
         if self.own is None:
@@ -252,10 +326,38 @@ class VocabParallelSampler:
     def __call__(self, logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
                  top_p: torch.Tensor, uniforms: Optional[torch.Tensor] = None,
                  penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
-                 rep_factor: Optional[torch.Tensor] = None, row_stats: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 rep_factor: Optional[torch.Tensor] = None, row_stats: Optional[torch.Tensor] = None,
+                 check_rows: bool = True) -> torch.Tensor:
         """logits: this rank's [B, vocab_local] slice.  Local candidates, the
         exchange, then the merge (with ``exchange="peer"``: one fused kernel);
-        returns the [B] ids (identical on every rank)."""
+        returns the [B] ids (identical on every rank).
+
+        With ``check_rows`` (outside CUDA-graph capture) the call waits for
+        the ids and raises ``VocabParallelError`` when a row came back -1;
+        a graph-replaying caller passes False and calls ``raise_on_failed``
+        on the ids it reads back."""
+        ids = self._step(logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats)
+        if check_rows and not torch.cuda.is_current_stream_capturing():
+            self.raise_on_failed(ids)
+        return ids
+
+    def raise_on_failed(self, ids) -> None:
+        """Raises ``VocabParallelError`` if any of the step's ids is -1 (reads
+        them back, and the exchange's error word)."""
+        got = ids.cpu() if torch.is_tensor(ids) else torch.as_tensor(ids)
+        bad = torch.nonzero(got.view(-1) < 0).view(-1).tolist()
+        if bad:
+            err = self.peer.error() if self.peer is not None else 0
+            why = ("a wait on another rank ran out (call reset() on every rank before the next step)" if err
+                   else "rows refused: top_k must lie in [1, cand_cap], or T <= 0")
+            raise VocabParallelError(f"rows {bad[:16]}{'...' if len(bad) > 16 else ''} came back -1: {why}")
+
+    def reset(self) -> int:
+        """After a VocabParallelError from a wait that ran out: clears the
+        error word and re-syncs the step counter on every rank (collective)."""
+        return self.peer.reset() if self.peer is not None else 0
+
+    def _step(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats):
         self._check(logits, temperature, top_k, top_p, uniforms)
         B = logits.shape[0]
         if self.peer is not None:

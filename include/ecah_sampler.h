@@ -272,6 +272,15 @@ ECAH_API int ecah_vp_ipc_alloc(size_t bytes, void** ptr, void* handle);
 ECAH_API int ecah_vp_ipc_open(const void* handle, void** ptr);
 ECAH_API int ecah_vp_ipc_close(void* ptr);
 ECAH_API int ecah_vp_ipc_free(void* ptr);
+/* Recovery after a step whose wait ran out (error word set), or after a rank
+ * skipped a step: writes this rank's exchange-buffer header to {epoch, 0
+ * finished rows, error 0} on `stream`.  The error word is sticky until then:
+ * every later step of this rank returns -1 for every row.  Call it on every
+ * rank with the same epoch -- the largest step counter over the ranks (the
+ * uint32 at byte 0 of each buffer) -- after a host barrier with no step in
+ * flight on any rank, then barrier again before the next step.  No
+ * counterpart in the reference, which runs on one GPU. */
+ECAH_API int ecah_vp_reset(void* own_buffer, uint32_t epoch, void* stream);
 
 #ifdef __cplusplus
 }

@@ -14,7 +14,7 @@ import torch
 from ecahlang_b200 import _abi
 from ecahlang_b200 import sampler as S
 from ecahlang_b200 import workloads as W
-from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
+from ecahlang_b200.vocab_parallel import VocabParallelError, VocabParallelSampler, split_vocab
 from gpu_util import BOUNDARY
 from oracle import sampler_oracle as so
 from vp_util import oracle_ids, vp_case
@@ -238,6 +238,70 @@ def test_vp_step_wait_runs_out_and_reports():
         assert (smp.out[:B].cpu() == -1).all()
         hdr = torch.as_tensor(_Raw(bufs[0], 64, "<i4"), device=dev).cpu()
         assert hdr[0] == 2 and hdr[2] == 1
+    finally:
+        torch.cuda.synchronize()
+        for p in bufs:
+            _abi.check(L.ecah_vp_ipc_free(p), "free")
+
+
+def test_vp_step_reset_then_resume():
+    """After a step whose waits ran out (sticky error word, every row -1),
+    ecah_vp_reset clears the error and sets the step counter; with the
+    stand-in rank 1 now flagging the next step (empty lists), the step
+    completes and draws exactly what ecah_vp_merge draws from rank 0's lists
+    and an empty rank 1."""
+    dev = torch.device("cuda")
+    B, V, world, cap = 8, 4000, 2, 64
+    x, T, K, P, U = vp_case(37, B, V)
+    T[:] = 1.0
+    K[:] = [1, 5, 20, 64, 65, 0, 3, 10]          # rows 4 and 5: refused (k > cap, no top-k)
+    off, loc = split_vocab(V, world, 0)
+    xd = torch.from_numpy(x[:, off:off + loc]).to(torch.bfloat16).to(dev).contiguous()
+    Td, Kd, Pd, Ud = (torch.from_numpy(a).to(dev) for a in (T, K, P, U))
+    smp = VocabParallelSampler(B, V, world, 0, torch.bfloat16, dev, seed=5, cand_cap=cap,
+                               exchange=lambda *a: None)
+    c_ref, n_ref = (t.clone() for t in smp.local(xd, Td, Kd, Pd))
+    L = _abi.lib()
+    nbytes = L.ecah_vp_exchange_bytes(B, world, cap)
+    bufs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        _abi.check(L.ecah_vp_ipc_alloc(nbytes, ctypes.byref(p), (ctypes.c_ubyte * 64)()), "alloc")
+        bufs.append(p.value)
+    lflag = 256
+    lcount = lflag + _al(4 * world * B)
+    try:
+        base = torch.tensor(bufs, dtype=torch.int64, device=dev)
+        peers = _abi.VPPeers(0, B, base.data_ptr(), 20000)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        a = smp._args(xd, Td, Kd, Pd, Ud, None, None, None, None)
+        _abi.check(L.ecah_vp_step(ctypes.byref(a), ctypes.byref(peers), stream), "ecah_vp_step")
+        torch.cuda.synchronize()
+        assert (smp.out[:B].cpu() == -1).all()
+        with pytest.raises(VocabParallelError):
+            smp.raise_on_failed(smp.out[:B])
+        hdr = torch.as_tensor(_Raw(bufs[0], 3, "<i4"), device=dev)
+        assert hdr.cpu().tolist() == [1, 0, 1]
+        _abi.check(L.ecah_vp_reset(bufs[0], 1, stream), "ecah_vp_reset")
+        torch.cuda.synchronize()
+        assert hdr.cpu().tolist() == [1, 0, 0]
+        # the stand-in rank 1 flags step 2 (parity 0) with empty lists
+        flags = torch.as_tensor(_Raw(bufs[0] + lflag, world * B, "<i4"), device=dev).view(world, B)
+        cnt = torch.as_tensor(_Raw(bufs[0] + lcount, 2 * world * B, "<i4"), device=dev).view(2, world, B)
+        cnt[0, 1].zero_()
+        flags[1].fill_(2)
+        torch.cuda.synchronize()
+        _abi.check(L.ecah_vp_step(ctypes.byref(a), ctypes.byref(peers), stream), "ecah_vp_step")
+        torch.cuda.synchronize()
+        got = smp.out[:B].cpu().clone()
+        assert hdr.cpu().tolist() == [2, 0, 0]
+        all_cand = torch.zeros(world, B, cap, dtype=torch.int64, device=dev)
+        all_count = torch.zeros(world, B, dtype=torch.int32, device=dev)
+        all_cand[0] = c_ref
+        all_count[0] = n_ref
+        want = smp.merge(all_cand, all_count, Td, Kd, Pd, uniforms=Ud).cpu()
+        assert torch.equal(got, want)
+        assert (got[[4, 5]] == -1).all() and int((got >= 0).sum()) >= 4   # the step resumed
     finally:
         torch.cuda.synchronize()
         for p in bufs:
