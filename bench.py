@@ -289,20 +289,22 @@ def run_native(a):
     rows_total = B * ws * a.steps
     value = rows_total / (ms / 1e3)
 
-    # ---- e2e through the public API: pinned host logits -> device -> sample -> ids on host
+    # ---- e2e through the drop-in API (SamplingManager, the reference manager's
+    # methods): parameters through its pinned buffers, pinned host logits ->
+    # device, sample, ids -> pinned host, every step
+    from ecahlang_b200.manager import SamplingManager
     host = w.logits.pin_memory()
-    hparams = [t.pin_memory() for t in (w.temperature, w.top_k, w.top_p)]
     dlog = torch.empty_like(bufs[0])
-    dparams = [torch.empty_like(t, device=dev) for t in hparams]
+    mgr = SamplingManager(V, seq_lens=B, dtype=w.logits.dtype, device=dev, seed=4321 + rank)
+    mgr.init_sampling_buffers(B)
+    Tl, Kl, Pl = w.temperature.numpy(), w.top_k.numpy(), w.top_p.numpy()
     ids_host = torch.empty(B, dtype=torch.int32).pin_memory()
     ke = max(3, min(a.steps, 50))
 
     def e2e_step():
+        mgr.fill_sampling_params(B, Tl, Kl, Pl)
         dlog.copy_(host, non_blocking=True)
-        for d, h in zip(dparams, hparams):
-            d.copy_(h, non_blocking=True)
-        out = smp(dlog, *dparams)
-        ids_host.copy_(out, non_blocking=True)
+        ids_host.copy_(mgr.sample(dlog), non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -321,7 +323,7 @@ def run_native(a):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ems = float(t.item())
     e2e_value = B * ws * ke / (ems / 1e3)
-    h2d = bytes_in + sum(t.numel() * t.element_size() for t in hparams)
+    h2d = bytes_in + 7 * 4 * B   # logits + the manager's seven parameter columns
 
     line = None
     if rank == 0:
@@ -342,7 +344,8 @@ def run_native(a):
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke},
+                    "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke,
+                    "api": "SamplingManager.fill_sampling_params + sample (pinned host buffers)"},
             # one sampler kernel per step; no other kernels run in the timed region
             "gpu_launches": a.steps,
             "clocks": clk.summary(),
@@ -363,11 +366,119 @@ def run_native(a):
                           f"(torch CPU port of the reference path, {threads} threads)",
                 "reference_logits_to_probs_c1": reference_logits_to_probs_c1()}
     del g_full, g_rem
+    # the other multi-GPU modes of configs[3] on the same ranks: the
+    # vocab-parallel step (the one that moves data between GPUs: the fused
+    # NVLink peer exchange) and the batch-sharded 8x batch
+    extra = {}
+    if not a.no_extra:
+        ms_c4b, b_c4 = c4_batch_measure(a, ws, rank, local, dev, min(a.steps, 200))
+        extra["batch_sharded_c4"] = {
+            "workload": "configs[3] at 8x the batch: B=4096 V=128256 bf16 (k=64, p=0.9), split over the ranks",
+            "rows_per_rank": b_c4, "us_per_step": 1e3 * ms_c4b, "rows_per_s": 4096 / (ms_c4b / 1e3),
+            "scaling": "strong", "note": "row kernel per rank, no collective"}
+        if ws > 1:
+            vp = vp_measure(a, ws, rank, local, dev, "peer", min(a.steps, 1000))
+            extra["vocab_parallel_c4"] = {
+                "workload": "configs[3]: B=512 V=128256 bf16 split by vocabulary, fused NVLink peer exchange",
+                "us_per_step": 1e3 * vp["ms_step"], "rows_per_s": vp["value"], "slice_per_rank": vp["loc"],
+                "cand_cap": vp["cap"], "exchange": vp["how"], "wait_timeouts": vp["err"],
+                "local_kernel_us": 1e3 * vp["ms_local"], "local_kernel_gbs": vp["roofline"]["achieved"],
+                "local_kernel_frac": vp["roofline"]["frac"], "scaling": "strong"}
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     if line is not None:
+        if extra:
+            line["extra"] = extra
         print(json.dumps(line), flush=True)
+
+
+def vp_measure(a, ws, rank, local, dev, exchange, steps):
+    """configs[3] vocab-parallel step on an initialised process group (or
+    one rank): B=512, V=128256 bf16 split by vocabulary; returns the timings
+    (max over ranks) and the rank-0 summary fields."""
+    from ecahlang_b200 import workloads as W
+    from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
+    w = W.config4(seed=0)
+    B, V = w.batch, w.vocab
+    off, loc = split_vocab(V, ws, rank)
+    bytes_in = B * loc * 2
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits[:, off:off + loc].contiguous().to(dev) for _ in range(nbuf)]
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    cap = min(256, 2048 // ws)
+    peer = exchange == "peer" and ws > 1
+    if peer:
+        exch = "peer"
+    elif ws > 1:
+        exch = None   # NCCL all-gather
+    else:
+        exch = lambda c, n, ac, an: (ac[0].copy_(c), an[0].copy_(n))
+    smp = VocabParallelSampler(B, V, ws, rank, torch.bfloat16, dev, seed=77, cand_cap=cap, exchange=exch)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(a.warmup):
+        smp(bufs[i % nbuf], T, K, P)
+    torch.cuda.synchronize()
+    chunk = min(steps, 2 * nbuf)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+
+    def capture(n, fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(n):
+                fn(i)
+        return g
+
+    g_full = capture(chunk, lambda i: smp(bufs[i % nbuf], T, K, P))
+    rem = steps % chunk
+    g_rem = capture(rem, lambda i: smp(bufs[i % nbuf], T, K, P)) if rem else None
+    g_full.replay()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(steps // chunk):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    err = smp.peer.error() if smp.peer is not None else 0
+    # the local kernel alone (the step's HBM pass), on this rank
+    g_loc = capture(chunk, lambda i: smp.local(bufs[i % nbuf], T, K, P))
+    g_loc.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    reps = max(1, min(20, steps // chunk))
+    for _ in range(reps):
+        g_loc.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / (reps * chunk)
+    if ws > 1:
+        t = torch.tensor([ms, ms_local, float(err)], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, ms_local, err = float(t[0].item()), float(t[1].item()), int(t[2].item())
+        torch.distributed.barrier()
+    del g_full, g_rem, g_loc
+    smp.close()
+    peak, peak_kind = _peaks()
+    how = ("fused kernel, lists stored into every rank's buffer over NVLink (CUDA IPC)" if peer else
+           "local kernel + NCCL all_gather + merge kernel" if ws > 1 else "local + merge kernels (1 rank)")
+    ms_step = ms / steps
+    achieved = bytes_in / (ms_local / 1e3) / 1e9
+    return {
+        "ms_step": ms_step, "value": B / (ms_step / 1e3), "B": B, "loc": loc, "cap": cap, "chunk": chunk,
+        "nbuf": nbuf, "how": how, "err": err, "ms_local": ms_local, "peer": peer, "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "local step (vp_local_row_kernel)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": bytes_in,
+                     "us_per_launch": 1e3 * ms_local},
+    }
 
 
 def run_vocab_parallel(a):
@@ -383,100 +494,70 @@ def run_vocab_parallel(a):
     if ws > 1:
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    from ecahlang_b200 import workloads as W
-    from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
-    w = W.config4(seed=0)
-    B, V = w.batch, w.vocab
-    off, loc = split_vocab(V, ws, rank)
-    bytes_in = B * loc * 2
-    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
-    bufs = [w.logits[:, off:off + loc].contiguous().to(dev) for _ in range(nbuf)]
-    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
-    cap = min(256, 2048 // ws)
-    peer = a.exchange == "peer" and ws > 1
-    if peer:
-        exch = "peer"
-    elif ws > 1:
-        exch = None   # NCCL all-gather
-    else:
-        exch = lambda c, n, ac, an: (ac[0].copy_(c), an[0].copy_(n))
-    smp = VocabParallelSampler(B, V, ws, rank, torch.bfloat16, dev, seed=77, cand_cap=cap, exchange=exch)
-    stream = torch.cuda.current_stream(dev)
-    for i in range(a.warmup):
-        smp(bufs[i % nbuf], T, K, P)
-    torch.cuda.synchronize()
-    chunk = min(a.steps, 2 * nbuf)
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(stream)
-
-    def capture(n, fn):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=side):
-            for i in range(n):
-                fn(i)
-        return g
-
-    g_full = capture(chunk, lambda i: smp(bufs[i % nbuf], T, K, P))
-    rem = a.steps % chunk
-    g_rem = capture(rem, lambda i: smp(bufs[i % nbuf], T, K, P)) if rem else None
-    g_full.replay()
-    torch.cuda.synchronize()
-    if ws > 1:
-        torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        for _ in range(a.steps // chunk):
-            g_full.replay()
-        if g_rem is not None:
-            g_rem.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    err = smp.peer.error() if smp.peer is not None else 0
-    # the local kernel alone (the step's HBM pass), on this rank
-    g_loc = capture(chunk, lambda i: smp.local(bufs[i % nbuf], T, K, P))
-    g_loc.replay()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    reps = max(1, min(20, a.steps // chunk))
-    for _ in range(reps):
-        g_loc.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_local = e0.elapsed_time(e1) / (reps * chunk)
-    if ws > 1:
-        t = torch.tensor([ms, ms_local, float(err)], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_local, err = float(t[0].item()), float(t[1].item()), int(t[2].item())
-        torch.distributed.barrier()
-    del g_full, g_rem, g_loc
-    smp.close()
+    r = vp_measure(a, ws, rank, local, dev, a.exchange, a.steps)
     if ws > 1:
         torch.distributed.destroy_process_group()
     if rank == 0:
-        ms_step = ms / a.steps
-        peak, peak_kind = _peaks()
-        alg = bytes_in   # per rank: its slice of the logits
-        achieved = alg / (ms_local / 1e3) / 1e9
-        how = ("fused kernel, lists stored into every rank's buffer over NVLink (CUDA IPC)" if peer else
-               "local kernel + NCCL all_gather + merge kernel" if ws > 1 else "local + merge kernels (1 rank)")
         print(json.dumps({
             "metric": "vocab-parallel sampler rows/sec (configs[3]: B=512, V=128256 bf16, k=64, p=0.9)",
-            "value": B / (ms_step / 1e3), "unit": "rows/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": ms_step, "us_per_step": 1e3 * ms_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "c4_vocab_parallel B=512 V=128256 bf16", "slice_per_rank": loc,
-                       "cand_cap": cap, "exchange": how, "launch": f"CUDA-graph replays of {chunk} steps",
-                       "l2": f"inputs rotate through {nbuf} device copies"},
-            "roofline": {"bound": "hbm", "kernel": "local step (vp_local_row_kernel)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": alg,
-                         "us_per_launch": 1e3 * ms_local},
-            "wait_timeouts": err,
-            "gpu_launches": a.steps * (1 if peer else 2),   # ours; NCCL and copy kernels not counted
-            "clocks": clk.summary(),
+            "value": r["value"], "unit": "rows/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": r["ms_step"], "us_per_step": 1e3 * r["ms_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "c4_vocab_parallel B=512 V=128256 bf16", "slice_per_rank": r["loc"],
+                       "cand_cap": r["cap"], "exchange": r["how"],
+                       "launch": f"CUDA-graph replays of {r['chunk']} steps",
+                       "l2": f"inputs rotate through {r['nbuf']} device copies"},
+            "roofline": r["roofline"],
+            "wait_timeouts": r["err"],
+            "gpu_launches": a.steps * (1 if r["peer"] else 2),   # ours; NCCL and copy kernels not counted
+            "clocks": r["clocks"],
         }), flush=True)
+
+
+def c4_batch_measure(a, ws, rank, local, dev, steps):
+    """configs[3]'s batch-sharded variant: the same rows at 8x the batch
+    (B = 4096 of V = 128256 bf16, k=64, p=0.9, T=1), split over the ranks;
+    each rank samples its 4096 / world rows with the row kernel, no
+    collective.  Returns (ms per step, max over ranks; rows per rank)."""
+    from ecahlang_b200 import sampler as S
+    from ecahlang_b200 import workloads as W
+    Bt = 4096
+    b = Bt // ws
+    w = W.config4(seed=rank, B=b)
+    V = w.vocab
+    bytes_in = b * V * 2
+    nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
+    bufs = [w.logits.to(dev) for _ in range(nbuf)]
+    T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    smp = S.Sampler(b, V, torch.bfloat16, dev, seed=99 + rank)
+    for i in range(a.warmup):
+        smp(bufs[i % nbuf], T, K, P)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for i in range(nbuf):
+            smp(bufs[i], T, K, P)
+    g.replay()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    reps = max(1, steps // nbuf)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * nbuf)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    return ms, b
 
 
 def run_decode(a):
@@ -721,6 +802,7 @@ def main():
                     help="reference: the CPU port of the reference path; flashinfer: the reference's "
                          "own GPU path (torch divides + FlashInfer sampling), for comparison")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="batch mode: skip the configs[3] lines")
     ap.add_argument("--mode", choices=["batch", "vp", "decode", "c3"], default="batch",
                     help="batch: configs[1], rows sharded over the ranks; vp: configs[3], vocabulary split; "
                          "decode: configs[4], µs the sampler adds to a graph-captured decode step; "
