@@ -565,8 +565,12 @@ def run_decode(a):
     Per concurrency B in {1, 8, 32, 128}: graph A = the LM head (fp16 GEMM,
     hidden 2048 -> V 151936, random-init weights N(0, 0.02^2) as the config's
     random-init model has, so the logits are nearly flat); graph B = the LM
-    head, then the sampler on its logits (T 0.7, top_p 0.9, as the config).
-    Added µs = B's replay time minus A's, CUDA events over graph replays.
+    head, then the drop-in sampling calls on its logits, as decode_forward's
+    graph would hold them: SamplingManager.sample (T 0.7, top_p 0.9, as the
+    config, with the requests' repetition-penalty histories) and
+    SamplingManager.update_penalties (ecahlang/main.py:159-171, :356-379,
+    :691-694).  Added µs = B's replay time minus A's, CUDA events over graph
+    replays.
     The 36 transformer layers before the head are not run: they do not touch
     the sampler's inputs, and the difference is what the sampler adds.  One
     GPU; other ranks exit."""
@@ -575,7 +579,7 @@ def run_decode(a):
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    from ecahlang_b200 import sampler as S
+    from ecahlang_b200.manager import SamplingManager
     H, V = 2048, 151936
     g = torch.Generator(device=dev).manual_seed(5)
     W = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(torch.float16)
@@ -588,17 +592,25 @@ def run_decode(a):
         for B in (1, 8, 32, 128):
             h = torch.randn(B, H, device=dev, generator=g).to(torch.float16)
             logits = torch.empty(B, V, device=dev, dtype=torch.float16)
-            T = torch.full((B,), 0.7, device=dev)
-            K = torch.zeros(B, dtype=torch.int32, device=dev)
-            P = torch.full((B,), 0.9, device=dev)
-            smp = S.Sampler(B, V, torch.float16, dev, seed=1)
+            # one request per row, each with a penalty slot (history capacity
+            # for the 384 tokens configs[4] generates), parameters through the
+            # bucket buffers
+            mgr = SamplingManager(V, seq_lens=B, dtype=torch.float16, device=dev, history_capacity=512, seed=1)
+            mgr.init_sampling_buffers(B)
+            mgr.init_cuda_graph_buffers([B])
+            reqs = [f"r{i}" for i in range(B)]
+            for r in reqs:
+                mgr.allocate(r)
+            mgr.fill_cuda_graph_sampling_params(B, B, [0.7] * B, [V] * B, [0.9] * B, rep_pens=[1.1] * B,
+                                                batch_ids=reqs)
 
             def head():
                 torch.matmul(h, W.t(), out=logits)
 
             def step():
                 head()
-                smp(logits, T, K, P)
+                ids = mgr.sample(logits, bucket_size=B)
+                mgr.update_penalties(ids, bucket_size=B)
 
             for _ in range(a.warmup):
                 step()
@@ -626,8 +638,9 @@ def run_decode(a):
         "metric": "µs the sampler adds to a CUDA-graph decode step (configs[4] shapes: LM head 2048 -> 151936 fp16)",
         "value": rows["128"]["us_added"], "unit": "us", "higher_is_better": False, "n_gpus": 1,
         "steps": reps * per_graph, "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "c5 decode step: LM head GEMM (+ sampler), random-init weights N(0, 0.02^2), "
-                               "T=0.7, top_p=0.9", "launch": f"CUDA-graph replays of {per_graph} steps"},
+        "config": {"workload": "c5 decode step: LM head GEMM (+ SamplingManager.sample + update_penalties), "
+                               "random-init weights N(0, 0.02^2), T=0.7, top_p=0.9, repetition penalty 1.1 "
+                               "with per-request histories", "launch": f"CUDA-graph replays of {per_graph} steps"},
         "per_concurrency": rows, "clocks": clk.summary(),
     }), flush=True)
 
