@@ -647,9 +647,9 @@ def run_decode(a):
 
 def run_c3(a):
     """B=128, V=151936 fp16, Zipf histories, T 0.8, top-p 0.95.
-    Two lines of one JSON object: the repetition penalty alone (the row
-    kernel; a wide nucleus, so the dense top-p path) and repetition +
-    frequency + presence penalties (the cluster kernel, 32-bit keys).  CUDA-
+    Two figures of one JSON object, both on the row kernel (a wide nucleus,
+    so the dense top-p path): the repetition penalty alone, and repetition +
+    frequency + presence penalties (the penalised logits stay fp16).  CUDA-
     graph replays over rotating input copies, CUDA events.  One GPU; other
     ranks exit."""
     ws, rank, local = _dist()

@@ -73,7 +73,7 @@ struct RSmem {
   // the row's repetition-penalty history bucketed by slice (round, warp):
   // slice s holds entries [poff[s], poff[s + 1]) of pent
   uint16_t poff[kMaxRounds * kNW + 1];
-  uint2 pent[kPenCap];            // {offset in the slice, divisor m as float bits}
+  uint2 pent[kPenCap];            // {offset in the slice | raw m << 16, additive term a as float bits}
   int pen_ok;                     // the buckets hold the whole history
 };
 
@@ -227,7 +227,8 @@ __device__ void complete_slice(const KParams& P, const RSmem& S, uint4* st, int 
       const int sl = r * kNW + (threadIdx.x >> 5);
       for (int i = S.poff[sl] + lane; i < S.poff[sl + 1]; i += 32) {
         const uint2 e = S.pent[i];
-        raw[e.x] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(Dt::to_f32(raw[e.x]), __uint_as_float(e.y)))));
+        const unsigned o = e.x & 0xFFFFu;
+        raw[o] = static_cast<uint16_t>(Dt::to_raw(penalise<DT>(Dt::to_f32(raw[o]), Dt::to_f32(e.x >> 16), __uint_as_float(e.y))));
       }
     } else {
       const int slot = P.row_slot[row];
@@ -240,7 +241,7 @@ __device__ void complete_slice(const KParams& P, const RSmem& S, uint4* st, int 
         if (cnt <= 0 || li < 0 || li >= n) continue;
         const float x = Dt::to_f32(raw[li]);
         const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
-        raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
+        raw[li] = static_cast<uint16_t>(Dt::to_raw(penalise<DT>(x, m, additive_term(P, row, cnt))));
       }
     }
     __syncwarp();
@@ -281,7 +282,10 @@ __device__ void bucket_penalties(const KParams& P, RSmem& S, int row, int& ph) {
       const int c = P.hist_cnt[base + h];
       if (c > 0 && tok >= 0 && tok < P.V) {
         const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(c, rf);
-        S.pent[atomicAdd(&cnt[tok / kWS], 1u)] = make_uint2(static_cast<unsigned>(tok % kWS), __float_as_uint(m));
+        // m is a model-dtype value: its 16-bit raw word rides beside the offset
+        S.pent[atomicAdd(&cnt[tok / kWS], 1u)] =
+            make_uint2(static_cast<unsigned>(tok % kWS) | (DType<DT>::to_raw(m) << 16),
+                       __float_as_uint(additive_term(P, row, c)));
       }
     }
   }
@@ -335,22 +339,22 @@ __device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], 
   for (int j = 0; j < 8; ++j) w[j] = keys2(raw[j]);
 }
 
-// the repetition-penalty patch of entries e0 .. e0+15 (values in yv)
+// the penalty patch of entries e0 .. e0+15 (values in yv)
 template <int DT>
 __device__ void patch16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
   if (!row_has_penalty(P, row)) return;
-  auto patch = [&](int li, float m) {
+  auto patch = [&](int li, float m, float a) {
 #pragma unroll
     for (int j = 0; j < kEPT; ++j)
-      if (j == li) yv[j] = DType<DT>::round(__fdiv_rn(yv[j], m));
+      if (j == li) yv[j] = penalise<DT>(yv[j], m, a);
   };
   if (S.pen_ok) {
     // entries e0 .. e0+15 lie in one slice: its bucket of the history
     const int sl = e0 / kWS, o0 = e0 % kWS;
     for (int i = S.poff[sl]; i < S.poff[sl + 1]; ++i) {
       const uint2 e = S.pent[i];
-      const int li = static_cast<int>(e.x) - o0;
-      if (li >= 0 && li < kEPT) patch(li, __uint_as_float(e.y));
+      const int li = static_cast<int>(e.x & 0xFFFFu) - o0;
+      if (li >= 0 && li < kEPT) patch(li, DType<DT>::to_f32(e.x >> 16), __uint_as_float(e.y));
     }
     return;
   }
@@ -362,7 +366,7 @@ __device__ void patch16(const KParams& P, const RSmem& S, int row, int e0, float
     const int li = P.hist_tok[hb + h] - P.vocab_offset - e0;
     const int cn = P.hist_cnt[hb + h];
     if (cn <= 0 || li < 0 || li >= kEPT || e0 + li >= P.V) continue;
-    patch(li, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf));
+    patch(li, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf), additive_term(P, row, cn));
   }
 }
 

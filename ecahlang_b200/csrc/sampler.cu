@@ -169,7 +169,7 @@ static bool row_layout(long long B, int V, RowLayout* L) {
 static bool k16_dtype(int dtype) { return dtype == ECAH_DTYPE_F16 || dtype == ECAH_DTYPE_BF16; }
 
 static bool make_plan(int dtype, int V, unsigned flags, Plan* p) {
-  const int kb = (dtype == ECAH_DTYPE_F32 || (flags & ECAH_FLAG_FREQ_PRES)) ? 32 : 16;
+  const int kb = (dtype == ECAH_DTYPE_F32) ? 32 : 16;   // additive penalties stay in the model dtype
   const int ksz = kb / 8;
   const int kpv = 16 / ksz;                       // keys per 16-byte vector
   const int target = (kb == 16) ? 20480 : 10240;  // keys per CTA aimed for (~40 KB)
@@ -306,7 +306,7 @@ int ecah_sampler_launch(const ecah_sampler_args* a, void* stream) {
   // row kernel: 16-bit keys; one CTA per row, or a row split over several
   // CTAs when the batch leaves SMs idle
   RowLayout L;
-  const bool k16 = k16_dtype(a->dtype) && !(a->flags & ECAH_FLAG_FREQ_PRES);
+  const bool k16 = k16_dtype(a->dtype);   // additive penalties keep the logits in the model dtype
   if (k16 && row_layout(a->batch, a->vocab, &L) && a->workspace_bytes >= L.total) {
     unsigned char* ws = static_cast<unsigned char*>(a->workspace);
     P.NC = L.NC;

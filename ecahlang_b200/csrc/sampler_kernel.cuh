@@ -108,6 +108,26 @@ __device__ __forceinline__ long long logits_row_offset(const KParams& P, int row
   return r * P.row_stride;
 }
 
+// One history entry's penalty applied to a model-dtype value x: the
+// repetition divide y = D(x / m), then, with ECAH_FLAG_FREQ_PRES, the additive
+// term a = f32(f32(f c) + pi) as y' = D(y - a) -- the penalised logit stays
+// in the model dtype, as the reference's `logits / mask_penalty` leaves it.
+template <int DT>
+__device__ __forceinline__ float penalise(float x, float m, float a) {
+  const float y = DType<DT>::round(__fdiv_rn(x, m));
+  return (a != 0.f) ? DType<DT>::round(__fsub_rn(y, a)) : y;
+}
+
+// The additive term of a history entry seen c > 0 times (0 without
+// ECAH_FLAG_FREQ_PRES): f32(f32(f c) + pi).
+__device__ __forceinline__ float additive_term(const KParams& P, int row, int c) {
+  if (!(P.flags & ECAH_FLAG_FREQ_PRES)) return 0.f;
+  const float f = P.freq_pen ? P.freq_pen[row] : 0.f;
+  const float pi = P.pres_pen ? P.pres_pen[row] : 0.f;
+  return __fadd_rn(__fmul_rn(f, static_cast<float>(c)), pi);
+}
+
+
 constexpr int kNB0 = 128;     // level-0 bins (7-bit digit), lane-private
 constexpr int kNBL = 512;     // bins of deeper levels / the key window
 constexpr int kWin = 512;     // keys in the window below the row max
@@ -497,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const KParams P) {
         const float x = Dt::to_f32(src[li]);
         const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
         float y = Dt::round(__fdiv_rn(x, m));
-        if (fp) y = __fsub_rn(y, __fadd_rn(__fmul_rn(fq, static_cast<float>(cnt)), pr));
+        // the additive term leaves the logit in the model dtype, as the divide does
+        if (fp) y = Dt::round(__fsub_rn(y, __fadd_rn(__fmul_rn(fq, static_cast<float>(cnt)), pr)));
         if constexpr (kRawInSmem) keys[li] = static_cast<Key>(Dt::to_raw(y));
         else keys[li] = static_cast<Key>(C::from_val(y));
       }

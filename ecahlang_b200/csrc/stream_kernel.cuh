@@ -84,7 +84,7 @@ __device__ void warp_select_seq(const T* hist, T target, int* out_bin, T* out_ab
 
 // ----------------------------------------------------------- chunk staging
 // Chunk c of `row` into `buf`: raw logits of the model dtype with the
-// repetition-penalty divide applied to the slot's history tokens; entries
+// slot's penalties applied to its history tokens (penalise); entries
 // past the row end read 0xFFFF (key 0, below every logit).
 //
 // issue_chunk starts the 16-byte cp.async copies of the whole vectors (no
@@ -122,7 +122,7 @@ __device__ void complete_chunk(const KParams& P, uint4* buf, int row, int c, int
         if (cnt <= 0 || li < 0 || li >= n) continue;
         const float x = Dt::to_f32(raw[li]);
         const float m = P.hist_mval ? P.hist_mval[base + h] : penalty_divisor<DT>(cnt, rf);
-        raw[li] = static_cast<uint16_t>(Dt::to_raw(Dt::round(__fdiv_rn(x, m))));
+        raw[li] = static_cast<uint16_t>(Dt::to_raw(penalise<DT>(x, m, additive_term(P, row, cnt))));
       }
     }
     __syncthreads();

@@ -64,7 +64,8 @@ enum ecah_status {
  *   y  = D(x / m(c))              repetition penalty, D = model dtype rounding,
  *                                 m(c) = mask value after c updates (hist_mval),
  *                                 m(c+1) = D(m(c) * rep_factor)
- *   y' = y - (f*c + pi) [c > 0]   only with ECAH_FLAG_FREQ_PRES (not in the reference)
+ *   y' = D(y - (f*c + pi)) [c > 0]   only with ECAH_FLAG_FREQ_PRES (not in the reference);
+ *                     the penalised logit stays in the model dtype D
  *   z  = y' / T                   float32; T <= 0 -> argmax (lowest index)
  *   top-k (k <= 0 or k >= vocab: off), ties with the k-th value kept
  *   softmax over the kept set, then top-p over it (p <= 0 or p >= 1: off)

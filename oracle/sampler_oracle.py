@@ -21,7 +21,9 @@ What it restates (per row r, token i, logits x in the model dtype D):
  3. Frequency / presence penalties (additive, OpenAI style).  NOT in the
     reference (ecahlang/parameters.py:4-12 exposes only repetition_penalty);
     applied only when the caller enables them:
-    ``y' = f32(y - f32(f32(f * c) + pi))`` for c > 0.  Parity unpinned.
+    ``y' = D(y - f32(f32(f * c) + pi))`` for c > 0: the penalised logit stays
+    in the model dtype D, as rule 2's divide leaves it (and as vLLM applies
+    these penalties to the logits tensor in its dtype).  Parity unpinned.
  4. ``z = f32(y') / T`` in float32 -- ``logits / temperature`` promotes to
     float32 (ecahlang/main.py:170, :399, :487, :580).  T <= 0 (only reachable
     by bypassing the request normalisation of ecahlang/main.py:642) is a pure
@@ -144,7 +146,7 @@ def penalised_logits(x, dtype, toks=None, cnts=None, mvals=None, rp=1.0,
     if freq_pres:
         pen = (np.float32(freq) * cnts.astype(np.float32)).astype(np.float32)
         pen = (pen + np.float32(pres)).astype(np.float32)
-        yv = (yv - pen).astype(np.float32)
+        yv = round_to((yv - pen).astype(np.float32), dtype)
     y[toks] = yv
     return y
 

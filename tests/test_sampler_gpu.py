@@ -101,8 +101,9 @@ def test_row_kernel_warp_regions_and_overflow():
 
 @pytest.mark.parametrize("use_mval", [True, False])
 def test_config3_penalised(use_mval):
-    """Zipf histories with repetition + frequency + presence penalties (32-bit
-    key path).  use_mval=False derives m(c) from the counts in the kernel."""
+    """Zipf histories with repetition + frequency + presence penalties (the
+    row kernel; the penalised logits stay fp16).  use_mval=False derives m(c)
+    from the counts in the kernel."""
     w = W.config3(seed=0, B=32)
     rp = w.rep_pen.numpy()
     hist = []
