@@ -384,6 +384,13 @@ def run_native(a):
                 "cand_cap": vp["cap"], "exchange": vp["how"], "wait_timeouts": vp["err"],
                 "local_kernel_us": 1e3 * vp["ms_local"], "local_kernel_gbs": vp["roofline"]["achieved"],
                 "local_kernel_frac": vp["roofline"]["frac"], "scaling": "strong"}
+            vq = vp_measure(a, ws, rank, local, dev, "peer", min(a.steps, 200), no_top_k=True)
+            extra["vocab_parallel_c4_no_top_k"] = {
+                "workload": "configs[3] with top-k off (top_k=0, p=0.9, T=1): B=512 V=128256 bf16 split by "
+                            "vocabulary; the rows take the exact distributed passes (5 slice passes, NCCL "
+                            "all-gather / all-reduce between them)",
+                "us_per_step": 1e3 * vq["ms_step"], "rows_per_s": vq["value"], "rows_refused": vq["rows_refused"],
+                "scaling": "strong"}
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -393,10 +400,12 @@ def run_native(a):
         print(json.dumps(line), flush=True)
 
 
-def vp_measure(a, ws, rank, local, dev, exchange, steps):
+def vp_measure(a, ws, rank, local, dev, exchange, steps, no_top_k=False):
     """configs[3] vocab-parallel step on an initialised process group (or
     one rank): B=512, V=128256 bf16 split by vocabulary; returns the timings
-    (max over ranks) and the rank-0 summary fields."""
+    (max over ranks) and the rank-0 summary fields.  no_top_k: every row
+    with top-k off (top_k = 0, p = 0.9 kept), drawn by the distributed passes
+    with NCCL collectives between them."""
     from ecahlang_b200 import workloads as W
     from ecahlang_b200.vocab_parallel import VocabParallelSampler, split_vocab
     w = W.config4(seed=0)
@@ -406,6 +415,10 @@ def vp_measure(a, ws, rank, local, dev, exchange, steps):
     nbuf = max(2, -(-3 * L2_BYTES // bytes_in))
     bufs = [w.logits[:, off:off + loc].contiguous().to(dev) for _ in range(nbuf)]
     T, K, P = w.temperature.to(dev), w.top_k.to(dev), w.top_p.to(dev)
+    full = None
+    if no_top_k:
+        K = torch.zeros_like(K)
+        full = torch.arange(B, dtype=torch.int32, device=dev)   # listed on the device: graph-capturable
     cap = min(256, 2048 // ws)
     peer = exchange == "peer" and ws > 1
     if peer:
@@ -417,7 +430,7 @@ def vp_measure(a, ws, rank, local, dev, exchange, steps):
     smp = VocabParallelSampler(B, V, ws, rank, torch.bfloat16, dev, seed=77, cand_cap=cap, exchange=exch)
     stream = torch.cuda.current_stream(dev)
     for i in range(a.warmup):
-        smp(bufs[i % nbuf], T, K, P)
+        smp(bufs[i % nbuf], T, K, P, full_rows=full)
     torch.cuda.synchronize()
     chunk = min(steps, 2 * nbuf)
     side = torch.cuda.Stream(dev)
@@ -430,11 +443,12 @@ def vp_measure(a, ws, rank, local, dev, exchange, steps):
                 fn(i)
         return g
 
-    g_full = capture(chunk, lambda i: smp(bufs[i % nbuf], T, K, P))
+    g_full = capture(chunk, lambda i: smp(bufs[i % nbuf], T, K, P, full_rows=full))
     rem = steps % chunk
-    g_rem = capture(rem, lambda i: smp(bufs[i % nbuf], T, K, P)) if rem else None
+    g_rem = capture(rem, lambda i: smp(bufs[i % nbuf], T, K, P, full_rows=full)) if rem else None
     g_full.replay()
     torch.cuda.synchronize()
+    bad = int((smp.out[:B] < 0).sum().item())   # rows drawn by neither path
     if ws > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -473,6 +487,7 @@ def vp_measure(a, ws, rank, local, dev, exchange, steps):
     achieved = bytes_in / (ms_local / 1e3) / 1e9
     return {
         "ms_step": ms_step, "value": B / (ms_step / 1e3), "B": B, "loc": loc, "cap": cap, "chunk": chunk,
+        "rows_refused": bad,
         "nbuf": nbuf, "how": how, "err": err, "ms_local": ms_local, "peer": peer, "clocks": clk.summary(),
         "roofline": {"bound": "hbm", "kernel": "local step (vp_local_row_kernel)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -25,7 +25,7 @@ EXPORTS = ("ecah_sampler_abi_version", "ecah_status_string", "ecah_sampler_works
            "ecah_sampler_launch_noalloc", "ecah_sampler_noalloc_scratch_bytes",
            "ecah_vp_local", "ecah_vp_merge", "ecah_vp_exchange_bytes", "ecah_vp_step",
            "ecah_vp_ipc_alloc", "ecah_vp_ipc_open", "ecah_vp_ipc_close", "ecah_vp_ipc_free",
-           "ecah_quotient_mismatches", "ecah_vp_reset")
+           "ecah_quotient_mismatches", "ecah_vp_reset", "ecah_vp_dist_pass")
 IPC_HANDLE_BYTES = 64
 
 
@@ -113,6 +113,9 @@ def lib():
         L.ecah_vp_ipc_close.restype = c_int32
         L.ecah_vp_ipc_close.argtypes = [c_void_p]
         L.ecah_vp_reset.restype = c_int32
+        L.ecah_vp_dist_pass.restype = c_int32
+        L.ecah_vp_dist_pass.argtypes = [ctypes.POINTER(VPArgs), c_int32, c_int32, c_void_p, c_int32, c_void_p,
+                                        c_void_p, c_void_p]
         L.ecah_vp_reset.argtypes = [c_void_p, c_uint32, c_void_p]
         L.ecah_vp_ipc_free.restype = c_int32
         L.ecah_vp_ipc_free.argtypes = [c_void_p]

@@ -11,6 +11,7 @@
 
 #include "row_kernel.cuh"
 #include "vp_kernel.cuh"
+#include "vp_dist.cuh"
 
 namespace ecah {
 
@@ -520,6 +521,51 @@ int ecah_vp_ipc_free(void* ptr) {
 int ecah_vp_reset(void* own_buffer, uint32_t epoch, void* stream) {
   if (!own_buffer) return ECAH_ERR_NULL;
   vp_reset_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<unsigned*>(own_buffer), epoch);
+  return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+}
+
+int ecah_vp_dist_pass(const ecah_vp_args* a, int32_t rank, int32_t pass, const int32_t* rows, int32_t nrows,
+                      const void* in, void* out, void* stream) {
+  const int st = vp_check(a);
+  if (st != ECAH_OK) return st;
+  const bool combine = pass >= 11 && pass <= 15;
+  if (!((pass >= 1 && pass <= 5) || combine) || nrows < 0 || rank < 0 || rank >= a->world) return ECAH_ERR_SHAPE;
+  if (nrows == 0) return ECAH_OK;
+  if (!rows || !out || (pass != 1 && !in)) return ECAH_ERR_NULL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (combine) {
+    if (pass == 15 && !a->out) return ECAH_ERR_NULL;
+    if (pass == 14 && !a->uniforms && !a->philox_state) return ECAH_ERR_NULL;
+    vd::CParams C = {};
+    C.temperature = a->temperature;
+    C.top_k = a->top_k;
+    C.top_p = a->top_p;
+    C.uniforms = a->uniforms;
+    C.philox_state = a->philox_state;
+    C.out = a->out;
+    C.B = a->batch;
+    C.vocab = a->vocab;
+    C.world = a->world;
+    C.rank = rank;
+    C.pass = pass - 10;
+    C.rows = rows;
+    C.n = nrows;
+    C.G = static_cast<const float*>(in);
+    C.S = static_cast<float*>(out);
+    vd::vp_dist_combine_kernel<<<nrows, 32, 0, s>>>(C);
+    return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
+  }
+  if (!a->logits) return ECAH_ERR_NULL;
+  if (a->row_slot && (!a->slot_len || !a->hist_tok || !a->hist_cnt || a->hist_cap < 0)) return ECAH_ERR_NULL;
+  vd::DParams D = {};
+  D.P = vp_kparams(a);
+  D.pass = pass;
+  D.rows = rows;
+  D.n = nrows;
+  D.gin = static_cast<const float*>(in);
+  D.gout = static_cast<float*>(out);
+  if (a->dtype == ECAH_DTYPE_F16) vd::vp_dist_kernel<ECAH_DTYPE_F16><<<nrows, vd::kDT, 0, s>>>(D);
+  else vd::vp_dist_kernel<ECAH_DTYPE_BF16><<<nrows, vd::kDT, 0, s>>>(D);
   return cudaGetLastError() == cudaSuccess ? ECAH_OK : ECAH_ERR_LAUNCH;
 }
 

@@ -10,7 +10,14 @@ whose key is at or above the slice's k-th largest key (ties included), in
 vocab order with global ids (``ecah_vp_local``); since the row's k-th largest
 key is at least every slice's, the union holds the row's whole top-k set, and
 ``ecah_vp_merge`` finishes the row exactly as the single-GPU sampler does.
-Rows need 1 <= top_k <= cand_cap (or T <= 0); other rows come back as -1.
+
+Rows without top-k (top_k <= 0 or >= vocab with T > 0: the reference's
+default request) keep more than any list holds; they take the exact
+distributed path (``ecah_vp_dist_pass``): five passes over the slices with a
+collective between each (the row max; the top-p threshold from two summed
+256-bin mass histograms, high key byte then low; each rank's kept mass, which
+names the rank that owns the draw; that rank's inverse CDF), every step
+decided on the device.  Rows with cand_cap < top_k < vocab come back -1.
 
 Two exchanges: ``exchange="peer"`` runs the whole step as one kernel per rank
 (``ecah_vp_step``) that stores each row's list straight into every rank's
@@ -52,6 +59,42 @@ def nccl_exchange(group=None) -> Callable[[torch.Tensor, torch.Tensor, torch.Ten
         dist.all_gather_into_tensor(all_cand.view(-1), cand.view(-1), group=group)
         dist.all_gather_into_tensor(all_count.view(-1), count.view(-1), group=group)
     return run
+
+
+class TorchCollectives:
+    """The collectives of the rows without top-k over a torch.distributed
+    group (NCCL over NVLink on GPUs): an all-gather in rank order into a flat
+    output, and an in-place all-reduce ("sum" or "max")."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(out, inp, group=self.group)
+
+    def all_reduce(self, t: torch.Tensor, op: str) -> None:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX, group=self.group)
+
+
+class _SingleRank:
+    """world == 1: the gathers are copies and the reductions are no-ops."""
+
+    def all_gather(self, out, inp):
+        out.copy_(inp)
+
+    def all_reduce(self, t, op):
+        pass
+
+
+class FullRowsStep:
+    """One step of the rows without top-k on one rank: the launch arguments
+    and the listed rows (built by ``VocabParallelSampler.full_rows_begin``)."""
+
+    def __init__(self, args, rows: torch.Tensor, n: int, keep):
+        self.args, self.rows, self.n = args, rows, n
+        self._keep = keep          # the tensors the arguments point at
 
 
 class VocabParallelError(RuntimeError):
@@ -214,7 +257,7 @@ class VocabParallelSampler:
 
     def __init__(self, max_batch: int, vocab: int, world: int, rank: int, dtype: torch.dtype,
                  device="cuda", seed: int = 0, cand_cap: int = 256,
-                 exchange=None, timeout_us: int = 1_000_000):
+                 exchange=None, timeout_us: int = 1_000_000, collectives=None):
         if dtype not in _DTYPES:
             raise RuntimeError(f"vocab-parallel sampling takes fp16/bf16 logits, not {dtype}")
         if world * cand_cap > 2048:
@@ -237,6 +280,10 @@ class VocabParallelSampler:
             self.exchange = None
         else:
             self.exchange = exchange if exchange is not None else nccl_exchange()
+        # rows without top-k: the exchanges between the distributed passes
+        self.collectives = collectives if collectives is not None else (
+            _SingleRank() if world == 1 else TorchCollectives())
+        self._fr = None
 
     def _args(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats):
         B = logits.shape[0]
@@ -323,20 +370,126 @@ class VocabParallelSampler:
               "ecah_vp_merge")
         return self.out[:B]
 
+    # ------------------------------------------------ rows without top-k
+    def _fr_buffers(self):
+        if self._fr is None:
+            mb, w, dev = self.cand.shape[0], self.world, self.device
+            f = dict(dtype=torch.float32, device=dev)
+            self._fr = {
+                "state": torch.zeros(mb, 8, **f), "rows": torch.zeros(mb, dtype=torch.int32, device=dev),
+                "u": torch.zeros(mb, **f),
+                1: torch.zeros(mb, 3, **f), "g1": torch.zeros(w * mb * 3, **f),
+                2: torch.zeros(mb, 256, **f), 3: torch.zeros(mb, 257, **f),
+                4: torch.zeros(mb, **f), "g4": torch.zeros(w * mb, **f),
+                5: torch.zeros(mb, dtype=torch.int32, device=dev),
+            }
+        return self._fr
+
+    def full_rows_begin(self, logits, temperature, top_k, top_p, rows, uniforms=None, penalty=None,
+                        row_slot=None, rep_factor=None) -> FullRowsStep:
+        """Sets up the distributed passes of one step for the listed rows
+        (host ints, or a device int32 tensor; rows with a top-k or T <= 0
+        are skipped on the device).  Without ``uniforms`` it writes this
+        step's Philox uniforms first, so call it before the candidate merge,
+        which advances the Philox state."""
+        self._check(logits, temperature, top_k, top_p, uniforms)
+        B = logits.shape[0]
+        fr = self._fr_buffers()
+        if torch.is_tensor(rows):
+            if rows.dtype != torch.int32 or rows.device != self.device or rows.dim() != 1:
+                raise RuntimeError("rows: expected a 1-d int32 tensor on the sampler's device")
+            rows_t = rows.contiguous()
+        else:
+            rows = list(rows)
+            if any(not 0 <= r < B for r in rows):
+                raise IndexError(f"rows must lie in [0, {B})")
+            rows_t = fr["rows"][: len(rows)]
+            rows_t.copy_(torch.tensor(rows, dtype=torch.int32))
+        n = rows_t.numel()
+        if n > self.cand.shape[0]:
+            raise RuntimeError(f"{n} rows exceed max_batch {self.cand.shape[0]}")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if uniforms is None:
+            uniforms = fr["u"][:B]
+            check(lib().ecah_philox_uniforms(self.philox_state.data_ptr(), B, uniforms.data_ptr(), 0, stream),
+                  "ecah_philox_uniforms")
+        a = self._args(logits, temperature.reshape(-1), top_k, top_p, uniforms, penalty, row_slot, rep_factor,
+                       None)
+        return FullRowsStep(a, rows_t, n, (logits, temperature, top_k, top_p, uniforms, penalty, row_slot,
+                                           rep_factor))
+
+    def full_rows_pass(self, st: FullRowsStep, p: int) -> torch.Tensor:
+        """Slice pass p (1..5) of the listed rows; returns this rank's
+        outputs ([n, 3], [n, 256], [n, 257], [n], [n] int32) for the
+        collective that follows."""
+        fr = self._fr_buffers()
+        out = fr[p][: st.n]
+        check(lib().ecah_vp_dist_pass(ctypes.byref(st.args), self.rank, p, st.rows.data_ptr(), st.n,
+                                      fr["state"].data_ptr(), out.data_ptr(),
+                                      torch.cuda.current_stream(self.device).cuda_stream), "ecah_vp_dist_pass")
+        return out
+
+    def full_rows_combine(self, st: FullRowsStep, p: int, combined: torch.Tensor) -> None:
+        """Folds the combined outputs of pass p into the row state (pass 1
+        and 4: gathered [world, n, ...] in rank order; 2 and 3: summed over
+        the ranks; 5: the max over the ranks, whose ids go to ``out``)."""
+        fr = self._fr_buffers()
+        if not combined.is_contiguous() or combined.device != self.device:
+            raise RuntimeError("combined outputs: expected a contiguous tensor on the sampler's device")
+        check(lib().ecah_vp_dist_pass(ctypes.byref(st.args), self.rank, 10 + p, st.rows.data_ptr(), st.n,
+                                      combined.data_ptr(), fr["state"].data_ptr(),
+                                      torch.cuda.current_stream(self.device).cuda_stream), "ecah_vp_dist_pass")
+
+    def full_rows_run(self, st: FullRowsStep, top_p_rows: bool = True) -> None:
+        """The passes with their collectives (``self.collectives``).  A row
+        without top-p has its draw's owner chosen from the pass-1 masses, so
+        passes 2-4 run only when a listed row may have 0 < top_p < 1."""
+        fr = self._fr_buffers()
+        n, w = st.n, self.world
+        for p in (1, 2, 3, 4, 5):
+            if p in (2, 3, 4) and not top_p_rows:
+                continue
+            o = self.full_rows_pass(st, p)
+            if p in (1, 4):
+                g = fr["g1" if p == 1 else "g4"][: w * o.numel()]
+                self.collectives.all_gather(g, o.reshape(-1))
+                combined = g
+            else:
+                self.collectives.all_reduce(o, "sum" if p in (2, 3) else "max")
+                combined = o
+            self.full_rows_combine(st, p, combined)
+
+    def find_full_rows(self, temperature, top_k, top_p):
+        """Host scan of the step's parameters (a device read): the rows
+        without top-k, and whether any of them has 0 < top_p < 1."""
+        T = temperature.reshape(-1).cpu()
+        K = top_k.cpu()
+        P = top_p.cpu()
+        sel = (T > 0) & ((K <= 0) | (K >= self.vocab))
+        rows = torch.nonzero(sel).view(-1).tolist()
+        return rows, bool(((P[sel] > 0) & (P[sel] < 1)).any()) if rows else False
+
     def __call__(self, logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
                  top_p: torch.Tensor, uniforms: Optional[torch.Tensor] = None,
                  penalty: Optional[PenaltyState] = None, row_slot: Optional[torch.Tensor] = None,
                  rep_factor: Optional[torch.Tensor] = None, row_stats: Optional[torch.Tensor] = None,
-                 check_rows: bool = True) -> torch.Tensor:
+                 check_rows: bool = True, full_rows=None) -> torch.Tensor:
         """logits: this rank's [B, vocab_local] slice.  Local candidates, the
         exchange, then the merge (with ``exchange="peer"``: one fused kernel);
         returns the [B] ids (identical on every rank).
+
+        Rows without top-k go through the distributed passes: ``full_rows``
+        lists them (host ints or a device int32 tensor; listing every row
+        is allowed, the others are skipped on the device).  Left as None, the
+        rows are found by reading the parameters back, outside CUDA-graph
+        capture; during capture they then come back -1.
 
         With ``check_rows`` (outside CUDA-graph capture) the call waits for
         the ids and raises ``VocabParallelError`` when a row came back -1;
         a graph-replaying caller passes False and calls ``raise_on_failed``
         on the ids it reads back."""
-        ids = self._step(logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats)
+        ids = self._step(logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats,
+                         full_rows)
         if check_rows and not torch.cuda.is_current_stream_capturing():
             self.raise_on_failed(ids)
         return ids
@@ -349,7 +502,8 @@ class VocabParallelSampler:
         if bad:
             err = self.peer.error() if self.peer is not None else 0
             why = ("a wait on another rank ran out (call reset() on every rank before the next step)" if err
-                   else "rows refused: top_k must lie in [1, cand_cap], or T <= 0")
+                   else "rows refused: cand_cap < top_k < vocab, a NaN logit, or a row without top-k "
+                        "that was not listed")
             raise VocabParallelError(f"rows {bad[:16]}{'...' if len(bad) > 16 else ''} came back -1: {why}")
 
     def reset(self) -> int:
@@ -357,23 +511,34 @@ class VocabParallelSampler:
         error word and re-syncs the step counter on every rank (collective)."""
         return self.peer.reset() if self.peer is not None else 0
 
-    def _step(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats):
+    def _step(self, logits, temperature, top_k, top_p, uniforms, penalty, row_slot, rep_factor, row_stats,
+              full_rows=None):
         self._check(logits, temperature, top_k, top_p, uniforms)
         B = logits.shape[0]
+        top_p_rows = True
+        if full_rows is None and not torch.cuda.is_current_stream_capturing():
+            full_rows, top_p_rows = self.find_full_rows(temperature, top_k, top_p)
+        fr = None
+        if full_rows is not None and len(full_rows) > 0:
+            fr = self.full_rows_begin(logits, temperature, top_k, top_p, full_rows, uniforms, penalty, row_slot,
+                                      rep_factor)
         if self.peer is not None:
             a = self._args(logits, temperature.reshape(-1), top_k, top_p, uniforms, penalty, row_slot,
                            rep_factor, row_stats)
             check(lib().ecah_vp_step(ctypes.byref(a), ctypes.byref(self.peer.peers),
                                      torch.cuda.current_stream(self.device).cuda_stream), "ecah_vp_step")
-            return self.out[:B]
-        cand, count = self.local(logits, temperature, top_k, top_p, penalty, row_slot, rep_factor)
-        if B == self.cand.shape[0]:
-            all_cand, all_count = self.all_cand, self.all_count
         else:
-            all_cand = self.all_cand.view(-1)[: self.world * B * self.cap].view(self.world, B, self.cap)
-            all_count = self.all_count.view(-1)[: self.world * B].view(self.world, B)
-        self.exchange(cand, count, all_cand, all_count)
-        return self.merge(all_cand, all_count, temperature, top_k, top_p, uniforms, row_stats)
+            cand, count = self.local(logits, temperature, top_k, top_p, penalty, row_slot, rep_factor)
+            if B == self.cand.shape[0]:
+                all_cand, all_count = self.all_cand, self.all_count
+            else:
+                all_cand = self.all_cand.view(-1)[: self.world * B * self.cap].view(self.world, B, self.cap)
+                all_count = self.all_count.view(-1)[: self.world * B].view(self.world, B)
+            self.exchange(cand, count, all_cand, all_count)
+            self.merge(all_cand, all_count, temperature, top_k, top_p, uniforms, row_stats)
+        if fr is not None:
+            self.full_rows_run(fr, top_p_rows)
+        return self.out[:B]
 
     def close(self) -> None:
         """Unmaps the peer exchange buffers (every rank, after its last step)."""

@@ -201,7 +201,8 @@ ECAH_API int ecah_quotient_mismatches(int32_t dtype, const float* temperature, i
  * all_cand/all_count; ecah_vp_merge then draws the same token on every rank
  * (the same uniforms / Philox state on every rank).  Rows need
  * 1 <= top_k <= cand_cap (or T <= 0); rows with top-k off, or whose lists
- * were truncated (count > cand_cap), get out = -1.  Replaces the whole-row FlashInfer call of
+ * were truncated (count > cand_cap), get out = -1 here; those without top-k
+ * are then drawn by ecah_vp_dist_pass.  Replaces the whole-row FlashInfer call of
  * ecahlang/main.py:377-379 when the LM head is split by vocabulary (ecahLang
  * itself runs on one GPU, ecahlang/env.py:112).
  */
@@ -241,6 +242,43 @@ typedef struct ecah_vp_args {
 
 ECAH_API int ecah_vp_local(const ecah_vp_args* args, void* stream);
 ECAH_API int ecah_vp_merge(const ecah_vp_args* args, void* stream);
+
+/* Rows without top-k (T > 0 and top_k <= 0 or >= vocab: the reference's
+ * default request, ecahlang/main.py:643, and top-p-only rows), whose kept set
+ * the candidate lists cannot hold: the exact distributed sampler, run over
+ * this rank's slice for the `nrows` batch rows listed in `rows` (device
+ * int32).  Listed rows that have a top-k or T <= 0 are skipped (their ids are
+ * left as they are), so a caller may list every row.  `state` is a device
+ * float [nrows, 8] per-row state.  pass selects one step:
+ *   1..5   (slice passes, in = state (unused by pass 1), out = the pass's
+ *           outputs, float [nrows, w]):
+ *     1  w = 3: {z of the slice max, lowest global id holding it, slice mass}
+ *     2  w = 256: masses (relative to the row max) per high byte of the key
+ *     3  w = 257: masses per low key byte inside the chosen high byte, and
+ *        [256] the mass above it
+ *     4  w = 1: the slice's kept mass (keys >= the top-p threshold's tie
+ *        floor and the zero-mass cut)
+ *     5  w = 1 (int32): on the rank that owns the draw, the lowest global id
+ *        whose cumulative kept mass in vocab order exceeds its target; -1
+ *        elsewhere
+ *   11..15 (combine after pass 1..5, in = the combined outputs, out = state):
+ *     11  in = pass 1 all-gathered [world, nrows, 3] (rank order)
+ *     12  in = pass 2 summed over the ranks [nrows, 256]
+ *     13  in = pass 3 summed over the ranks [nrows, 257]
+ *     14  in = pass 4 all-gathered [world, nrows]; the uniform is
+ *         uniforms[row], else the Philox uniform of the current state
+ *     15  in = pass 5 max over the ranks [nrows] (int32): writes out[row]
+ *         (-1 for a row with a NaN logit).
+ * So one step runs 1, all-gather, 11, 2, all-reduce, 12, 3, all-reduce, 13,
+ * 4, all-gather, 14, 5, all-reduce (max), 15.  Combine 11 already chooses
+ * the owning rank of a row without top-p (its kept set is every entry above
+ * the zero-mass cut), and passes 2-4 skip such rows: when no listed row has
+ * 0 < top_p < 1 the step is 1, all-gather, 11, 5, all-reduce (max), 15.  Keys are the
+ * order-preserving 16-bit keys of the penalised logits; the top-p threshold
+ * is the reference's (the largest z whose mass from the top reaches
+ * top_p * Z).  New entry point: the reference runs on one GPU. */
+ECAH_API int ecah_vp_dist_pass(const ecah_vp_args* args, int32_t rank, int32_t pass, const int32_t* rows,
+                               int32_t nrows, const void* in, void* out, void* stream);
 
 /*
  * The whole vocab-parallel step in one kernel per rank, with the exchange

@@ -70,6 +70,9 @@ def test_vp_config4_rows_match_oracle(world):
 
 
 def test_vp_rows_without_top_k_are_refused():
+    """The candidate path alone refuses rows without top-k (their kept set
+    exceeds any list); the distributed passes serve them
+    (test_vp_full_rows_gpu.py)."""
     dev = torch.device("cuda")
     B, V = 8, 4000
     x, T, K, P, U = vp_case(2, B, V)
@@ -168,6 +171,11 @@ def _nccl_rank(rank, world, port, outdir):
         Td, Kd, Pd, Ud = (torch.from_numpy(a).to(dev) for a in (T, K, P, U))
         ids = smp(xd, Td, Kd, Pd, uniforms=Ud)
         np.save(os.path.join(outdir, f"nccl{rank}.npy"), ids.cpu().numpy())
+        # rows without top-k: the distributed passes over NCCL
+        K2 = K.copy()
+        K2[0::3] = 0
+        ids = smp(xd, Td, torch.from_numpy(K2).to(dev), Pd, uniforms=Ud)
+        np.save(os.path.join(outdir, f"full{rank}.npy"), ids.cpu().numpy())
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -376,4 +384,10 @@ def test_vp_two_nccl_ranks(tmp_path):
     near = np.array([rr.u_margin < BOUNDARY or rr.p_margin < BOUNDARY for rr in res.rows])
     a, b = np.load(tmp_path / "nccl0.npy"), np.load(tmp_path / "nccl1.npy")
     assert np.array_equal(a, b)
+    assert np.array_equal(a[~near], want[~near])
+    K[0::3] = 0
+    want, res = oracle_ids(x, T, K, P, U)
+    near = np.array([rr.u_margin < BOUNDARY or rr.p_margin < BOUNDARY for rr in res.rows])
+    a, b = np.load(tmp_path / "full0.npy"), np.load(tmp_path / "full1.npy")
+    assert np.array_equal(a, b) and (a >= 0).all()
     assert np.array_equal(a[~near], want[~near])
