@@ -74,6 +74,8 @@ struct RSmem {
   // slice s holds entries [poff[s], poff[s + 1]) of pent
   uint16_t poff[kMaxRounds * kNW + 1];
   uint2 pent[kPenCap];            // {offset in the slice | raw m << 16, additive term a as float bits}
+  unsigned long long pre[2];      // the Philox state and
+  float upre;                     //   the caller's uniform, copied in while the row streams
   int pen_ok;                     // the buckets hold the whole history
 };
 
@@ -339,10 +341,12 @@ __device__ __forceinline__ void round_load(const uint4* st, uint32_t (&raw)[8], 
   for (int j = 0; j < 8; ++j) w[j] = keys2(raw[j]);
 }
 
-// the penalty patch of entries e0 .. e0+15 (values in yv)
-template <int DT>
+// the penalty patch of entries e0 .. e0+15 (values in yv); KNOWN: the
+// caller has established that the row has a history (which otherwise costs
+// two dependent global loads per call)
+template <int DT, bool KNOWN = false>
 __device__ void patch16(const KParams& P, const RSmem& S, int row, int e0, float (&yv)[kEPT]) {
-  if (!row_has_penalty(P, row)) return;
+  if (!KNOWN && !row_has_penalty(P, row)) return;
   auto patch = [&](int li, float m, float a) {
 #pragma unroll
     for (int j = 0; j < kEPT; ++j)
@@ -378,6 +382,34 @@ __device__ void load16(const KParams& P, const RSmem& S, int row, int e0, float 
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) yv[j] = (e0 + j < P.V) ? DType<DT>::to_f32(src[e0 + j]) : __int_as_float(0x7FC00000);
   patch16<DT>(P, S, row, e0, yv);
+}
+
+// The raw word of entry e of the row with the penalty patch applied (one
+// lane's share of a chunk that a warp reads entry by entry).
+template <int DT>
+__device__ uint32_t patched_raw(const KParams& P, const RSmem& S, int row, int e) {
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row);
+  const uint32_t raw = src[e];
+  if (!row_has_penalty(P, row)) return raw;
+  float y = DType<DT>::to_f32(raw);
+  if (S.pen_ok) {
+    const int sl = e / kWS, o = e % kWS;
+    for (int i = S.poff[sl]; i < S.poff[sl + 1]; ++i) {
+      const uint2 en = S.pent[i];
+      if (static_cast<int>(en.x & 0xFFFFu) == o) y = penalise<DT>(y, DType<DT>::to_f32(en.x >> 16), __uint_as_float(en.y));
+    }
+  } else {
+    const int slot = P.row_slot[row];
+    const int len = min(P.slot_len[slot], P.hist_cap);
+    const float rf = P.rep_factor ? P.rep_factor[row] : 1.0f;
+    const long long hb = static_cast<long long>(slot) * P.hist_cap;
+    for (int h = 0; h < len; ++h) {
+      const int cn = P.hist_cnt[hb + h];
+      if (cn > 0 && P.hist_tok[hb + h] - P.vocab_offset == e)
+        y = penalise<DT>(y, P.hist_mval ? P.hist_mval[hb + h] : penalty_divisor<DT>(cn, rf), additive_term(P, row, cn));
+    }
+  }
+  return DType<DT>::to_raw(y);
 }
 
 // The raw words of entries e0 .. e0+15 (e0 a multiple of 16): two 16-byte
@@ -1044,7 +1076,7 @@ __device__ __forceinline__ void patch_chunk(const KParams& P, const RSmem& S, in
   float yv[kEPT];
 #pragma unroll
   for (int j = 0; j < kEPT; ++j) yv[j] = DType<DT>::to_f32((j & 1) ? (wv[j >> 1] >> 16) : (wv[j >> 1] & 0xFFFFu));
-  patch16<DT>(P, S, row, e0, yv);
+  patch16<DT, true>(P, S, row, e0, yv);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const uint32_t lo = (e0 + 2 * j < P.V) ? DType<DT>::to_raw(yv[2 * j]) : 0xFFFFu;
@@ -1232,6 +1264,334 @@ __device__ __forceinline__ LeanRes lean_finish(const KParams& P, RSmem& S, int r
   res.result = S.ib[4];
   res.Z = Z;
   res.key_lo_k = key_lo_k;
+  res.key_lo = key_lo;
+  res.kdraw = kdraw;
+  return res;
+}
+
+// ------------------------------------------------ top-p rows finished from chunk records
+// Unsplit rows with top-p and no top-k keep no candidates while streaming.
+// For every chunk of 16 entries the stream records its two largest keys
+// (top1 | top2 << 16; chunk c = r kT + t as for top-k records), in the ckey
+// and cidx regions, while it sums the row's masses per segment as usual.
+constexpr int kRec2Rounds = kCB * (sizeof(uint16_t) + sizeof(uint32_t)) / sizeof(uint32_t) / kT;   // 12
+__device__ __forceinline__ uint32_t* recs2(RSmem& S) { return reinterpret_cast<uint32_t*>(S.ckey); }
+
+// The two largest of a thread's 16 keys (8 packed words, 2 keys each) as
+// top1 | top2 << 16.  Each half runs a tournament keeping its two largest
+// (the second of a merge of sorted pairs (a1 >= a2), (b1 >= b2) is
+// max(min(a1, b1), max(a2, b2))), then the halves merge the same way.
+__device__ __forceinline__ uint32_t top2_16(const uint32_t (&w)[8]) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    h[q] = max16x2(w[2 * q], w[2 * q + 1]);
+    l[q] = min16x2(w[2 * q], w[2 * q + 1]);
+  }
+  const uint32_t H01 = max16x2(h[0], h[1]), L01 = max16x2(min16x2(h[0], h[1]), max16x2(l[0], l[1]));
+  const uint32_t H23 = max16x2(h[2], h[3]), L23 = max16x2(min16x2(h[2], h[3]), max16x2(l[2], l[3]));
+  const uint32_t H = max16x2(H01, H23), L = max16x2(min16x2(H01, H23), max16x2(L01, L23));
+  const uint32_t a1 = H & 0xFFFFu, b1 = H >> 16, a2 = L & 0xFFFFu, b2 = L >> 16;
+  return max(a1, b1) | (max(min(a1, b1), max(a2, b2)) << 16);
+}
+
+// The first bin b (four per thread, bin 4 tid + j) where the running sum of
+// m4 over bins in order reaches target, given this thread's exclusive prefix
+// ex and the block total tot.  When rounding keeps every thread's running sum
+// short although tot reaches the target, the last non-zero bin.  INT_MAX
+// when tot stays below the target.  Every thread gets the result.
+__device__ __forceinline__ int cross_bin(const float (&m4)[4], float s4, float ex, float tot, float target, RSmem& S,
+                                         int& ph) {
+  const int tid = threadIdx.x;
+  int mine = INT_MAX;
+  if (s4 > 0.f && ex + s4 >= target) {
+    float acc = ex;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (mine == INT_MAX && m4[j] > 0.f && acc + m4[j] >= target) mine = tid * 4 + j;
+      acc += m4[j];
+    }
+    if (mine == INT_MAX) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (m4[j] > 0.f) mine = tid * 4 + j;
+    }
+  }
+  unsigned bsel = rmin_u(static_cast<unsigned>(mine), S, ph);
+  if (bsel == static_cast<unsigned>(INT_MAX) && tot >= target) {
+    int last = -1;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (m4[j] > 0.f) last = tid * 4 + j;
+    bsel = static_cast<unsigned>(static_cast<int>(rmax_u(static_cast<unsigned>(last + 1), S, ph)) - 1);
+  }
+  if (tot < target || bsel == 0xFFFFFFFFu) return INT_MAX;
+  return static_cast<int>(bsel);
+}
+
+// The records' counts per key live in S.lp, a histogram of kPleanNB bins that
+// the stream fills as it records: bin h holds key hwhi - h, where hwhi is
+// round 0's max plus kPleanHead (the row max is almost always within that
+// headroom; when it is not, the finish histograms the records again).
+constexpr int kPleanHead = 512;
+constexpr int kPleanNB = kHB + kPleanHead;
+
+// counts a thread's two records (top1 | top2 << 16) into the histogram
+__device__ __forceinline__ void plean_count(RSmem& S, uint32_t t12, uint32_t hwhi) {
+  const uint32_t t1 = t12 & 0xFFFFu, t2 = t12 >> 16;
+  const uint32_t d1 = hwhi - t1, d2 = hwhi - t2;   // keys above hwhi wrap past the bins
+  if (d1 < static_cast<uint32_t>(kPleanNB) && t1 != 0u) atomicAdd(&S.lp[d1], 1u);
+  if (d2 < static_cast<uint32_t>(kPleanNB) && t2 != 0u) atomicAdd(&S.lp[d2], 1u);
+}
+
+// Finish scratch in the stages (after the stream), in 4-byte words: the mass
+// of each of the 4096 keys under the row max, then (sized once the count n of
+// re-read chunks is known) the list of those chunks, their kept masses and a
+// cache of their 16 entries.
+constexpr int kPleanListOff = kHB;                      // words
+constexpr int kStageWords = kStages * kRVecs * 4;
+
+// Top-p threshold and draw of a record row, without re-streaming it.
+//   1. The records alone bound the mass at or above each key from below:
+//      every record is an entry.  bL = the first bin where that lower bound
+//      reaches p S; the kept set's lowest key tau_p is then at or above
+//      v = kmax - bL.  When the records hold less than p S in the window but
+//      at least half of it (a wide nucleus), v is the window's lowest key.
+//   2. An entry at or above v that is not a record lies in a chunk whose
+//      top2 is at or above v.  Those chunks (listed in vocab order) are
+//      re-read from L2, spread evenly over the threads: their entries at or
+//      above v are added to the histogram and their two records taken out,
+//      which leaves exact counts in every bin up to bL (any other chunk's
+//      entries at or above v are its top1 alone).
+//   3. tau_p from those exact counts, as on the candidate path; then each
+//      re-read chunk's kept mass, again spread evenly.
+//   4. The draw in vocab order: thread t owns chunks [R t, R t + R); a
+//      re-read chunk contributes its kept mass, any other its top1 when kept.
+//      The thread holding u Z finds the chunk where the running sum crosses
+//      u Z, and warp 0 reads that chunk entry by entry (a top1 is unique in
+//      its chunk, or the chunk's top2 would equal it and the chunk would have
+//      been re-read).
+// The per-bin masses of the bound and of the exact counts are summed in the
+// same order, and an exact count is never below the records' count of its
+// bin, so the exact running sum reaches p S no later than bin bL.  Returns
+// ok = false (nothing decided) when neither bound applies, or the exact
+// counts do not reach p S (a nucleus wider than the window), or tau_p lands
+// below v after the tie floor.
+template <int DT>
+__device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int row, int R, uint32_t kmax, float M,
+                                             float T, float rT, float pp, float S_all, uint32_t key_cut, float u,
+                                             uint32_t hwhi, int& ph) {
+  using C = Codec<DT, 16>;
+  const int tid = threadIdx.x;
+  LeanRes res{false, 0, 0.f, 0u, 0u, 0u};
+  const uint32_t* rec = recs2(S);
+  unsigned* cL = S.lp;
+  unsigned* sw = reinterpret_cast<unsigned*>(&S.stage[0][0]);
+  float* mt = reinterpret_cast<float*>(sw);
+  const uint32_t klo = (kmax >= static_cast<uint32_t>(kHB)) ? kmax - static_cast<uint32_t>(kHB - 1) : 1u;
+  const int nch = (P.V + kEPT - 1) / kEPT;
+
+  // bin b (key kmax - b) of the histogram is cL[b + hoff]
+  uint32_t hoff = hwhi - kmax;
+  if (kmax > hwhi) {
+    // the row max lies above the stream's window: count the records again
+    for (int i = tid; i < kPleanNB; i += kT) cL[i] = 0u;
+    __syncthreads();
+    for (int r = 0; r < R; ++r) {
+      const uint32_t rv = rec[r * kT + tid];
+      const uint32_t t1 = rv & 0xFFFFu, t2 = rv >> 16;
+      if (t1 >= klo) atomicAdd(&cL[kmax - t1], 1u);
+      if (t2 >= klo) atomicAdd(&cL[kmax - t2], 1u);
+    }
+    hoff = 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = tid * 4 + j;
+    mt[b] = (kmax - static_cast<uint32_t>(b) >= klo && kmax >= static_cast<uint32_t>(b))
+                ? mass_of(C::value(kmax - static_cast<uint32_t>(b)), T, rT, M) : 0.f;
+  }
+  __syncthreads();
+
+  // ---- 1. the records' lower bound
+  const float target = __fmul_rn(pp, S_all);
+  float m4[4];
+  float s4 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = tid * 4 + j;
+    m4[j] = __fmul_rn(static_cast<float>(cL[b + hoff]), mt[b]);
+    s4 += m4[j];
+  }
+  float tot;
+  float ex = rscan_f(s4, S, ph, &tot);
+  int bL = cross_bin(m4, s4, ex, tot, target, S, ph);
+  if (bL == INT_MAX) {
+    if (!(tot >= 0.5f * target)) return res;
+    bL = static_cast<int>(kmax - klo);
+  }
+  const uint32_t v = kmax - static_cast<uint32_t>(bL);
+
+  // ---- 2. chunks that may hold unrecorded entries at or above v
+  const int c0 = tid * R, c1 = min(c0 + R, nch);
+  int nf = 0;
+  for (int c = c0; c < c1; ++c) nf += (rec[c] >> 16) >= v ? 1 : 0;
+  int n;
+  const int o0 = rscan_i(nf, S, ph, &n);
+  uint16_t* list = reinterpret_cast<uint16_t*>(sw + kPleanListOff);
+  float* imass = reinterpret_cast<float*>(sw + kPleanListOff + ((n + 7) / 8) * 4);
+  uint4* cache = reinterpret_cast<uint4*>(sw + kPleanListOff + ((n + 7) / 8) * 4 + ((n + 3) / 4) * 4);
+  const int cap = (kStageWords - (kPleanListOff + ((n + 7) / 8) * 4 + ((n + 3) / 4) * 4)) / 8;   // chunks
+  const bool cached = n <= cap;
+  {
+    int o = o0;
+    for (int c = c0; c < c1; ++c)
+      if ((rec[c] >> 16) >= v) list[o++] = static_cast<uint16_t>(c);
+  }
+  __syncthreads();
+  const bool pen = row_has_penalty(P, row);
+  // Listed chunks come in through the cache in waves of at most cap, every
+  // thread's copies in flight together; item i of a wave sits in slot i - w0.
+  auto fetch_wave = [&](int w0, int w1) {
+    for (int i = w0 + tid; i < w1; i += kT) {
+      const int e0 = static_cast<int>(list[i]) * kEPT;
+      uint4* d = cache + 2 * (i - w0);
+      if (P.vec_ok && e0 + kEPT <= P.V) {
+        const uint4* g = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + e0);
+        cp_async16(d, g);
+        cp_async16(d + 1, g + 1);
+      } else {
+        chunk_raw(P, row, e0, d[0], d[1]);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+  };
+  for (int w0 = 0; w0 < n; w0 += cap) {
+    const int w1 = min(n, w0 + cap);
+    fetch_wave(w0, w1);
+    for (int i = w0 + tid; i < w1; i += kT) {
+      uint4 ca = cache[2 * (i - w0)], cb = cache[2 * (i - w0) + 1];
+      const int c = list[i];
+      if (pen) {
+        patch_chunk<DT>(P, S, row, c * kEPT, ca, cb);
+        cache[2 * (i - w0)] = ca;
+        cache[2 * (i - w0) + 1] = cb;
+      }
+      for (uint32_t m = chunk_mask(ca, cb, v); m; m &= m - 1u)
+        atomicAdd(&cL[kmax - key16(raw_at(ca, cb, __ffs(m) - 1)) + hoff], 1u);
+      const uint32_t rv = rec[c];
+      atomicSub(&cL[kmax - (rv & 0xFFFFu) + hoff], 1u);
+      atomicSub(&cL[kmax - (rv >> 16) + hoff], 1u);
+    }
+    __syncthreads();
+  }
+
+  // ---- 3. tau_p from the exact counts of the bins at or above v
+  s4 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int b = tid * 4 + j;
+    m4[j] = (b <= bL) ? __fmul_rn(static_cast<float>(cL[b + hoff]), mt[b]) : 0.f;
+    s4 += m4[j];
+  }
+  ex = rscan_f(s4, S, ph, &tot);
+  const int bs = cross_bin(m4, s4, ex, tot, target, S, ph);
+  if (bs == INT_MAX) return res;
+  const uint32_t key_lo = tie_floor<DT, 16>(kmax - static_cast<uint32_t>(bs), T);
+  if (key_lo < v) return res;
+  const uint32_t kdraw = max(key_lo, key_cut);
+  // each listed chunk's kept mass (a single wave is still in the cache, patched)
+  for (int w0 = 0; w0 < n; w0 += cap) {
+    const int w1 = min(n, w0 + cap);
+    if (!cached) fetch_wave(w0, w1);
+    for (int i = w0 + tid; i < w1; i += kT) {
+      uint4 ca = cache[2 * (i - w0)], cb = cache[2 * (i - w0) + 1];
+      if (pen && !cached) patch_chunk<DT>(P, S, row, static_cast<int>(list[i]) * kEPT, ca, cb);
+      float sm = 0.f;
+      for (uint32_t m = chunk_mask(ca, cb, kdraw); m; m &= m - 1u) sm += mt[kmax - key16(raw_at(ca, cb, __ffs(m) - 1))];
+      imass[i] = sm;
+    }
+    __syncthreads();
+  }
+
+  // ---- 4. the draw over this thread's chunks, in vocab order
+  float wsum = 0.f;
+  {
+    int i = o0;
+    for (int c = c0; c < c1; ++c) {
+      const uint32_t rv = rec[c];
+      if ((rv >> 16) >= v) wsum += imass[i++];
+      else if ((rv & 0xFFFFu) >= kdraw) wsum += mt[kmax - (rv & 0xFFFFu)];
+    }
+  }
+  float Z;
+  ex = rscan_f(wsum, S, ph, &Z);
+  const float tgt = __fmul_rn(u, Z);
+  const unsigned mine = (wsum > 0.f && ex + wsum > tgt) ? static_cast<unsigned>(tid) : static_cast<unsigned>(INT_MAX);
+  unsigned pick, lastp;
+  rminmax_u(mine, wsum > 0.f ? static_cast<unsigned>(tid + 1) : 0u, S, ph, &pick, &lastp);
+  if (pick == static_cast<unsigned>(INT_MAX) && lastp == 0u) return res;
+  const bool take_last = pick == static_cast<unsigned>(INT_MAX);
+  const int owner = take_last ? static_cast<int>(lastp) - 1 : static_cast<int>(pick);
+  if (tid == owner) {
+    // the same sums in the same order: the chunk where ex + (running sum)
+    // crosses the target, or the last with kept mass
+    float run = ex, base = ex;
+    int hc = -1, hi = -1, i = o0;
+    for (int c = c0; c < c1; ++c) {
+      const uint32_t rv = rec[c];
+      float add = 0.f;
+      int ii = -1;
+      if ((rv >> 16) >= v) { ii = i++; add = imass[ii]; }
+      else if ((rv & 0xFFFFu) >= kdraw) add = mt[kmax - (rv & 0xFFFFu)];
+      if (add > 0.f) {
+        hc = c; hi = ii; base = run;
+        run += add;
+        if (!take_last && run > tgt) break;
+      }
+    }
+    S.ib[5] = hc;
+    S.ib[6] = hi;
+    S.fb[5] = base;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // warp 0 reads that chunk, one entry per lane: a re-read chunk's kept
+    // masses summed over the lanes in order (its last kept entry when
+    // rounding keeps the running sum short); a top1 located in its chunk
+    const int hc = S.ib[5], hi = S.ib[6], lane = tid;
+    int e = -1;
+    if (hc >= 0) {
+      const int ej = hc * kEPT + lane;
+      uint32_t key = 0u;
+      if (lane < kEPT && ej < P.V)
+        key = key16((hi >= 0 && cached) ? static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(cache + 2 * hi)[lane])
+                                        : patched_raw<DT>(P, S, row, ej));
+      if (hi >= 0) {
+        const float m = (lane < kEPT && key >= kdraw) ? mt[kmax - key] : 0.f;
+        float incl = m;
+#pragma unroll
+        for (int o = 1; o < kEPT; o <<= 1) {
+          const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const unsigned hit = __ballot_sync(0xFFFFFFFFu, !take_last && m > 0.f && S.fb[5] + incl > tgt);
+        const unsigned nz = __ballot_sync(0xFFFFFFFFu, m > 0.f);
+        e = hc * kEPT + (hit ? __ffs(hit) - 1 : (nz ? 31 - __clz(nz) : 0));
+      } else {
+        const unsigned b = __ballot_sync(0xFFFFFFFFu, lane < kEPT && key == (rec[hc] & 0xFFFFu));
+        e = hc * kEPT + (b ? __ffs(b) - 1 : 0);
+      }
+    }
+    if (lane == 0) S.ib[4] = e;
+  }
+  __syncthreads();
+  res.ok = S.ib[4] >= 0;
+  res.result = S.ib[4];
+  res.Z = Z;
+  res.key_lo_k = 0u;
   res.key_lo = key_lo;
   res.kdraw = kdraw;
   return res;
@@ -1577,6 +1937,10 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     // unsplit top-k rows record chunk top keys instead of keeping
     // candidates (lean_finish)
     const bool lean = !SPLIT && !VPL && N > 0 && topk && R <= kRecRounds;
+    // unsplit top-p rows without top-k record each chunk's two largest keys
+    // (plean_finish)
+    const bool plean = !SPLIT && !VPL && mass_all && topp && R <= kRec2Rounds;
+    if (plean) N = 0;
 
     // running state
     unsigned best = 0u;       // thread max key
@@ -1585,7 +1949,21 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     int fill = 0;
     bool overflow = (N == 0);
 
+    // the row's uniform (or the Philox state) lands in shared memory with
+    // thread 0's first stream copies, so it is there when the row finishes
+    // (the vocabulary-parallel steps draw elsewhere and may pass neither)
+    if (!VPL && tid == 0 && sampled) {
+      if (P.uniforms) {
+        cp_async4(&S.upre, P.uniforms + row);
+      } else if (P.philox_state) {
+        cp_async8(&S.pre[0], P.philox_state);
+        cp_async8(&S.pre[1], P.philox_state + 1);
+      }
+    }
     if (row_has_penalty(P, row)) bucket_penalties<DT>(P, S, row, ph);
+    uint32_t hwhi = 0u;       // record rows: top of the records' histogram
+    if (plean)
+      for (int i = tid; i < kPleanNB; i += kT) S.lp[i] = 0u;   // the stream's first barrier orders it
     uint32_t kcut = 0u;       // mass rows: warps whose keys all lie below skip their masses
     const uint32_t kinf = C::from_val(INFINITY), kninf = C::from_val(-INFINITY);
 
@@ -1594,10 +1972,19 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     // candidates), so each mode's stream loop carries only its own work.
     auto round_body = [&](auto mode, int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) {
       constexpr int MD = decltype(mode)::value;
-      constexpr bool kMass = (MD & 1) != 0, kCand = (MD & 4) != 0, kRec = (MD & 8) != 0;   // bit 1: segment masses (the same code)
-      const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
-                                  max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
-      const uint32_t tm = max(m2 & 0xFFFFu, m2 >> 16);   // padding keys are 0
+      // bit 1: segment masses (the same code); bit 3: top-key records; bit 4: top-two records
+      constexpr bool kMass = (MD & 1) != 0, kCand = (MD & 4) != 0, kRec = (MD & 8) != 0, kRec2 = (MD & 16) != 0;
+      uint32_t tm;   // padding keys are 0
+      if constexpr (kRec2) {
+        const uint32_t t12 = top2_16(w);
+        recs2(S)[(r - r0) * kT + tid] = t12;
+        tm = t12 & 0xFFFFu;
+        if (r != r0) plean_count(S, t12, hwhi);   // round r0's wait for the window
+      } else {
+        const uint32_t m2 = max16x2(max16x2(max16x2(w[0], w[1]), max16x2(w[2], w[3])),
+                                    max16x2(max16x2(w[4], w[5]), max16x2(w[6], w[7])));
+        tm = max(m2 & 0xFFFFu, m2 >> 16);
+      }
       if constexpr (kRec) recs(S)[(r - r0) * kT + tid] = static_cast<uint16_t>(tm);
       if (tm > best) { best = tm; bround = r; }
       uint32_t k0 = 0u;  // max of the part's first round (that round only)
@@ -1636,6 +2023,13 @@ __device__ __forceinline__ void row_body(const KParams& P) {
         }
         const float ws = warp_sum(rs);
         if (lane == 0) { S.ss[r * kNW + warp] = ws; S.sq[r * kNW + warp] = cq; }
+      }
+      if constexpr (kRec2) {
+        if (r == r0) {
+          // the records' histogram covers keys up to round 0's max plus kPleanHead
+          hwhi = min(k0 + static_cast<uint32_t>(kPleanHead), 0xFFFFu);
+          plean_count(S, recs2(S)[tid], hwhi);
+        }
       }
 
       if constexpr (kCand) {
@@ -1728,7 +2122,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       }
     };
     using std::integral_constant;
-    const int smode = lean ? 8 : ((mass_all ? 1 : 0) | (segs ? 2 : 0) | (!overflow ? 4 : 0));
+    const int smode = lean ? 8 : (plean ? 17 : ((mass_all ? 1 : 0) | (segs ? 2 : 0) | (!overflow ? 4 : 0)));
 #define ECAH_ROUND(M) stream_row<DT>(P, S, row, r0, r1, [&](int r, const uint4* st, uint32_t (&raw)[8], uint32_t (&w)[8], int nv) { round_body(integral_constant<int, M>{}, r, st, raw, w, nv); })
     switch (smode) {
       case 0: ECAH_ROUND(0); break;
@@ -1737,6 +2131,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
       case 4: ECAH_ROUND(4); break;
       case 5: ECAH_ROUND(5); break;
       case 8: ECAH_ROUND(8); break;
+      case 17: ECAH_ROUND(17); break;
       default: ECAH_ROUND(7); break;   // no row mode sets other bits together
     }
 #undef ECAH_ROUND
@@ -1801,11 +2196,7 @@ __device__ __forceinline__ void row_body(const KParams& P) {
     const bool greedy = !(T > 0.f) || !isfinite(M);
     int result = static_cast<int>(first == 0xFFFFFFFFu ? 0u : first);
     RowFin* fin = static_cast<RowFin*>(P.ws_fin) + row;
-    float u = 0.f;
-    if (!greedy) {
-      if (P.uniforms) u = P.uniforms[row];
-      else u = row_uniform(__ldcg(&P.philox_state[0]), __ldcg(&P.philox_state[1]), static_cast<uint64_t>(row));
-    }
+    const float u = greedy ? 0.f : (P.uniforms ? S.upre : row_uniform(S.pre[0], S.pre[1], static_cast<uint64_t>(row)));
 
     if (greedy) {
       if (tid == 0) {
@@ -1858,6 +2249,16 @@ __device__ __forceinline__ void row_body(const KParams& P) {
           lean_result = lr.result;
         } else {
           fast = false;   // the re-streaming paths below
+        }
+      }
+      if (plean && mass_ok) {
+        const LeanRes lr = plean_finish<DT>(P, S, row, R, kmax, M, T, rT, pp, S_all, key_cut, u, hwhi, ph);
+        if (lr.ok) {
+          lean_done = true;
+          fast = true;
+          key_lo = lr.key_lo;
+          lean_Z = lr.Z;
+          lean_result = lr.result;
         }
       }
       if (thr) {
