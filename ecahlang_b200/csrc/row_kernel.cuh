@@ -1355,16 +1355,15 @@ constexpr int kStageWords = kStages * kRVecs * 4;
 //   1. The records alone bound the mass at or above each key from below:
 //      every record is an entry.  bL = the first bin where that lower bound
 //      reaches p S; the kept set's lowest key tau_p is then at or above
-//      v = kmax - bL.  When the records hold less than p S in the window but
-//      at least half of it (a wide nucleus), v is the window's lowest key.
+//      v = kmax - bL.
 //   2. An entry at or above v that is not a record lies in a chunk whose
 //      top2 is at or above v.  Those chunks (listed in vocab order) are
-//      re-read from L2, spread evenly over the threads: their entries at or
+//      copied from L2 into shared memory, all at once: their entries at or
 //      above v are added to the histogram and their two records taken out,
 //      which leaves exact counts in every bin up to bL (any other chunk's
 //      entries at or above v are its top1 alone).
 //   3. tau_p from those exact counts, as on the candidate path; then each
-//      re-read chunk's kept mass, again spread evenly.
+//      re-read chunk's kept mass.
 //   4. The draw in vocab order: thread t owns chunks [R t, R t + R); a
 //      re-read chunk contributes its kept mass, any other its top1 when kept.
 //      The thread holding u Z finds the chunk where the running sum crosses
@@ -1374,9 +1373,9 @@ constexpr int kStageWords = kStages * kRVecs * 4;
 // The per-bin masses of the bound and of the exact counts are summed in the
 // same order, and an exact count is never below the records' count of its
 // bin, so the exact running sum reaches p S no later than bin bL.  Returns
-// ok = false (nothing decided) when neither bound applies, or the exact
-// counts do not reach p S (a nucleus wider than the window), or tau_p lands
-// below v after the tie floor.
+// ok = false (nothing decided) when the bound does not reach p S within the
+// window, the listed chunks outgrow the shared-memory cache (a wide
+// nucleus), or tau_p lands below v after the tie floor.
 template <int DT>
 __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int row, int R, uint32_t kmax, float M,
                                              float T, float rT, float pp, float S_all, uint32_t key_cut, float u,
@@ -1425,11 +1424,8 @@ __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int 
   }
   float tot;
   float ex = rscan_f(s4, S, ph, &tot);
-  int bL = cross_bin(m4, s4, ex, tot, target, S, ph);
-  if (bL == INT_MAX) {
-    if (!(tot >= 0.5f * target)) return res;
-    bL = static_cast<int>(kmax - klo);
-  }
+  const int bL = cross_bin(m4, s4, ex, tot, target, S, ph);
+  if (bL == INT_MAX) return res;
   const uint32_t v = kmax - static_cast<uint32_t>(bL);
 
   // ---- 2. chunks that may hold unrecorded entries at or above v
@@ -1441,8 +1437,9 @@ __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int 
   uint16_t* list = reinterpret_cast<uint16_t*>(sw + kPleanListOff);
   float* imass = reinterpret_cast<float*>(sw + kPleanListOff + ((n + 7) / 8) * 4);
   uint4* cache = reinterpret_cast<uint4*>(sw + kPleanListOff + ((n + 7) / 8) * 4 + ((n + 3) / 4) * 4);
-  const int cap = (kStageWords - (kPleanListOff + ((n + 7) / 8) * 4 + ((n + 3) / 4) * 4)) / 8;   // chunks
-  const bool cached = n <= cap;
+  // a nucleus so wide that its chunks outgrow the cache goes to the
+  // re-streaming paths, which handle it at less cost than re-reading them
+  if (n > (kStageWords - (kPleanListOff + ((n + 7) / 8) * 4 + ((n + 3) / 4) * 4)) / 8) return res;
   {
     int o = o0;
     for (int c = c0; c < c1; ++c)
@@ -1450,43 +1447,36 @@ __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int 
   }
   __syncthreads();
   const bool pen = row_has_penalty(P, row);
-  // Listed chunks come in through the cache in waves of at most cap, every
-  // thread's copies in flight together; item i of a wave sits in slot i - w0.
-  auto fetch_wave = [&](int w0, int w1) {
-    for (int i = w0 + tid; i < w1; i += kT) {
-      const int e0 = static_cast<int>(list[i]) * kEPT;
-      uint4* d = cache + 2 * (i - w0);
-      if (P.vec_ok && e0 + kEPT <= P.V) {
-        const uint4* g = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + e0);
-        cp_async16(d, g);
-        cp_async16(d + 1, g + 1);
-      } else {
-        chunk_raw(P, row, e0, d[0], d[1]);
-      }
+  // the listed chunks come in through the cache, every thread's copies in
+  // flight together; item i sits in slot i
+  for (int i = tid; i < n; i += kT) {
+    const int e0 = static_cast<int>(list[i]) * kEPT;
+    uint4* d = cache + 2 * i;
+    if (P.vec_ok && e0 + kEPT <= P.V) {
+      const uint4* g = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + e0);
+      cp_async16(d, g);
+      cp_async16(d + 1, g + 1);
+    } else {
+      chunk_raw(P, row, e0, d[0], d[1]);
     }
-    cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
-  };
-  for (int w0 = 0; w0 < n; w0 += cap) {
-    const int w1 = min(n, w0 + cap);
-    fetch_wave(w0, w1);
-    for (int i = w0 + tid; i < w1; i += kT) {
-      uint4 ca = cache[2 * (i - w0)], cb = cache[2 * (i - w0) + 1];
-      const int c = list[i];
-      if (pen) {
-        patch_chunk<DT>(P, S, row, c * kEPT, ca, cb);
-        cache[2 * (i - w0)] = ca;
-        cache[2 * (i - w0) + 1] = cb;
-      }
-      for (uint32_t m = chunk_mask(ca, cb, v); m; m &= m - 1u)
-        atomicAdd(&cL[kmax - key16(raw_at(ca, cb, __ffs(m) - 1)) + hoff], 1u);
-      const uint32_t rv = rec[c];
-      atomicSub(&cL[kmax - (rv & 0xFFFFu) + hoff], 1u);
-      atomicSub(&cL[kmax - (rv >> 16) + hoff], 1u);
-    }
-    __syncthreads();
   }
+  cp_async_wait_all();
+  __syncthreads();
+  for (int i = tid; i < n; i += kT) {
+    uint4 ca = cache[2 * i], cb = cache[2 * i + 1];
+    const int c = list[i];
+    if (pen) {
+      patch_chunk<DT>(P, S, row, c * kEPT, ca, cb);
+      cache[2 * i] = ca;
+      cache[2 * i + 1] = cb;
+    }
+    for (uint32_t m = chunk_mask(ca, cb, v); m; m &= m - 1u)
+      atomicAdd(&cL[kmax - key16(raw_at(ca, cb, __ffs(m) - 1)) + hoff], 1u);
+    const uint32_t rv = rec[c];
+    atomicSub(&cL[kmax - (rv & 0xFFFFu) + hoff], 1u);
+    atomicSub(&cL[kmax - (rv >> 16) + hoff], 1u);
+  }
+  __syncthreads();
 
   // ---- 3. tau_p from the exact counts of the bins at or above v
   s4 = 0.f;
@@ -1502,19 +1492,14 @@ __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int 
   const uint32_t key_lo = tie_floor<DT, 16>(kmax - static_cast<uint32_t>(bs), T);
   if (key_lo < v) return res;
   const uint32_t kdraw = max(key_lo, key_cut);
-  // each listed chunk's kept mass (a single wave is still in the cache, patched)
-  for (int w0 = 0; w0 < n; w0 += cap) {
-    const int w1 = min(n, w0 + cap);
-    if (!cached) fetch_wave(w0, w1);
-    for (int i = w0 + tid; i < w1; i += kT) {
-      uint4 ca = cache[2 * (i - w0)], cb = cache[2 * (i - w0) + 1];
-      if (pen && !cached) patch_chunk<DT>(P, S, row, static_cast<int>(list[i]) * kEPT, ca, cb);
-      float sm = 0.f;
-      for (uint32_t m = chunk_mask(ca, cb, kdraw); m; m &= m - 1u) sm += mt[kmax - key16(raw_at(ca, cb, __ffs(m) - 1))];
-      imass[i] = sm;
-    }
-    __syncthreads();
+  // each listed chunk's kept mass, from the cache (patched)
+  for (int i = tid; i < n; i += kT) {
+    const uint4 ca = cache[2 * i], cb = cache[2 * i + 1];
+    float sm = 0.f;
+    for (uint32_t m = chunk_mask(ca, cb, kdraw); m; m &= m - 1u) sm += mt[kmax - key16(raw_at(ca, cb, __ffs(m) - 1))];
+    imass[i] = sm;
   }
+  __syncthreads();
 
   // ---- 4. the draw over this thread's chunks, in vocab order
   float wsum = 0.f;
@@ -1567,8 +1552,8 @@ __device__ __forceinline__ LeanRes plean_finish(const KParams& P, RSmem& S, int 
       const int ej = hc * kEPT + lane;
       uint32_t key = 0u;
       if (lane < kEPT && ej < P.V)
-        key = key16((hi >= 0 && cached) ? static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(cache + 2 * hi)[lane])
-                                        : patched_raw<DT>(P, S, row, ej));
+        key = key16(hi >= 0 ? static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(cache + 2 * hi)[lane])
+                            : patched_raw<DT>(P, S, row, ej));
       if (hi >= 0) {
         const float m = (lane < kEPT && key >= kdraw) ? mt[kmax - key] : 0.f;
         float incl = m;

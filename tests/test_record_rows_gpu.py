@@ -2,7 +2,7 @@
 per-chunk records (the two largest keys of every 16 entries) instead of a
 candidate buffer.  Batches of 40 rows and more run one unsplit CTA per row on
 148 SMs, which is where those rows take the record path; the cases cover the
-re-read list in and beyond its shared-memory cache, chunks whose two largest
+re-read list within and beyond its shared-memory cache, chunks whose two largest
 keys tie, penalised rows, odd vocabulary sizes around the record capacity
 (12 rounds of 16384 entries) and rows whose nucleus the records cannot place
 (they fall back to the re-streaming paths)."""
@@ -68,9 +68,10 @@ def test_record_top_p_ties_in_chunks():
 
 
 def test_record_top_p_wide_nucleus():
-    """C3's wide Gaussian (no shifted group) at T = 0.8 and p = 0.95: some
-    thousand chunks hold a second nucleus entry, more than the cache holds,
-    so the listed chunks are read twice from L2."""
+    """C3's wide Gaussian (no shifted group): at T = 0.8 and p = 0.95 some
+    thousand chunks hold a second nucleus entry, more than the shared-memory
+    cache holds, so those rows leave the record path for the re-streaming
+    paths; narrower nuclei (lower p or T) stay on it."""
     B, V = 48, W.V_QWEN
     g = torch.Generator().manual_seed(73)
     x = (torch.randn(B, V, generator=g) * 2.5).half()
