@@ -113,6 +113,9 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
   using Dt = DType<DT>;
   __shared__ __align__(16) uint16_t raw[kDCH];
   __shared__ float hist[257];
+  // pass 2: per high key byte, 16 lane columns (lanes l and l + 16 share
+  // one), so the lanes of a warp never pile onto one bin's address
+  __shared__ float lpm[256 * 16];
   __shared__ float red[kDT / 32];
   __shared__ unsigned ured[kDT / 32];
   const KParams& P = D.P;
@@ -203,6 +206,8 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
       return;
     }
     for (int b = tid; b < 257; b += kDT) hist[b] = 0.f;
+    if (D.pass == 2)
+      for (int b = tid; b < 256 * 16; b += kDT) lpm[b] = 0.f;
     float above = 0.f;
     __syncthreads();
     for (int c0 = 0; c0 < V; c0 += kDCH) {
@@ -216,7 +221,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
         if (D.pass == 3 && kh < hb) continue;
         const float ms = mass_of(Dt::to_f32(raw[e]), T, rT, M);
         if (!(ms > 0.f)) continue;
-        if (D.pass == 2) atomicAdd(&hist[kh], ms);
+        if (D.pass == 2) atomicAdd(&lpm[(kh << 4) | (tid & 15)], ms);
         else if (kh == hb) atomicAdd(&hist[key & 255u], ms);
         else above += ms;
       }
@@ -225,6 +230,14 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     if (D.pass == 3) {
       const float a = bsum(above, red);
       if (tid == 0) hist[256] = a;
+    } else {
+      // the lane columns of each bin, in column order
+      for (int b = tid; b < 256; b += kDT) {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) t += lpm[(b << 4) | c];
+        hist[b] = t;
+      }
     }
     __syncthreads();
     const int width = (D.pass == 2) ? 256 : 257;
