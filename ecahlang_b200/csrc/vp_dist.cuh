@@ -35,8 +35,8 @@ namespace ecah {
 namespace vd {
 
 constexpr int kDT = 256;
-constexpr int kDCH = 8192;               // entries per staged chunk
-constexpr int kDPer = kDCH / kDT;        // 32 consecutive entries per thread
+constexpr int kDCH = 4096;               // entries per staged chunk (two buffers)
+constexpr int kDPer = kDCH / kDT;        // 16 consecutive entries per thread
 
 // per-row state between passes
 constexpr int kState = 8;
@@ -62,19 +62,28 @@ struct DParams {
   float* gout;                           // [n, width] outputs (pass 5: int ids)
 };
 
-// Chunk c of the slice of `row` into raw (16-bit words), penalty patched; 0xFFFF
-// (key 0) past the slice end.
+// Pipelined staging: the vector part of the next chunk is copied in (cp.async,
+// one commit group per chunk) while the current chunk is counted; two
+// buffers alternate.  stage_issue starts chunk [c0, c0 + len) into buf;
+// stage_finish waits for it (the next chunk's group may stay in flight),
+// then loads the scalar rest, pads past the slice end and applies the
+// penalty patch, as stage does.
 template <int DT>
-__device__ void stage(const KParams& P, uint16_t* raw, int row, int c0, int len) {
-  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + c0;
-  int done = 0;
-  if (P.vec_ok) {   // 16-byte loads of the whole vectors (c0 is a multiple of 8)
+__device__ __forceinline__ void stage_issue(const KParams& P, uint16_t* buf, int row, int c0, int len) {
+  if (P.vec_ok && len > 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + c0);
+    uint4* r4 = reinterpret_cast<uint4*>(buf);
     const int nv = len >> 3;
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* r4 = reinterpret_cast<uint4*>(raw);
-    for (int v = threadIdx.x; v < nv; v += kDT) r4[v] = __ldg(s4 + v);
-    done = nv << 3;
+    for (int v = threadIdx.x; v < nv; v += kDT) cp_async16(r4 + v, s4 + v);
   }
+  cp_async_commit();
+}
+
+template <int DT>
+__device__ void stage_finish(const KParams& P, uint16_t* raw, int row, int c0, int len) {
+  cp_async_wait_group<1>();
+  const uint16_t* src = static_cast<const uint16_t*>(P.logits) + logits_row_offset(P, row) + c0;
+  const int done = P.vec_ok ? ((len >> 3) << 3) : 0;
   for (int i = done + threadIdx.x; i < kDCH; i += kDT) raw[i] = (i < len) ? src[i] : static_cast<uint16_t>(0xFFFFu);
   __syncthreads();
   if (P.row_slot) {
@@ -91,8 +100,26 @@ __device__ void stage(const KParams& P, uint16_t* raw, int row, int c0, int len)
         raw[li] = static_cast<uint16_t>(DType<DT>::to_raw(penalise<DT>(DType<DT>::to_f32(raw[li]), m, 0.f)));
       }
     }
+    __syncthreads();
   }
-  __syncthreads();
+}
+
+// the chunk loop: fn(raw, c0, len) counts a staged chunk; it returns false
+// to stop early (every thread the same), after which no copy stays in flight
+template <int DT, typename Fn>
+__device__ __forceinline__ void stream_slice(const KParams& P, uint16_t (*bufs)[kDCH], int row, int V, Fn&& fn) {
+  stage_issue<DT>(P, bufs[0], row, 0, min(kDCH, V));
+  int k = 0;
+  for (int c0 = 0; c0 < V; c0 += kDCH, ++k) {
+    const int len = min(kDCH, V - c0);
+    if (c0 + kDCH < V) stage_issue<DT>(P, bufs[(k + 1) & 1], row, c0 + kDCH, min(kDCH, V - c0 - kDCH));
+    else cp_async_commit();   // an empty group keeps the count of groups in flight
+    stage_finish<DT>(P, bufs[k & 1], row, c0, len);
+    const bool more = fn(bufs[k & 1], c0, len);
+    __syncthreads();          // the buffer is refilled two chunks on
+    if (!more) break;
+  }
+  cp_async_wait_group<0>();
 }
 
 __device__ __forceinline__ float bsum(float v, float* red) {
@@ -111,10 +138,10 @@ template <int DT>
 __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DParams D) {
   using C = Codec<DT, 16>;
   using Dt = DType<DT>;
-  __shared__ __align__(16) uint16_t raw[kDCH];
+  __shared__ __align__(16) uint16_t rawb[2][kDCH];
   __shared__ float hist[257];
   // pass 2: per high key byte, 16 lane columns (lanes l and l + 16 share
-  // one), so the lanes of a warp never pile onto one bin's address
+  // one), so the lanes of a warp do not pile onto one bin's address
   __shared__ float lpm[256 * 16];
   __shared__ float red[kDT / 32];
   __shared__ unsigned ured[kDT / 32];
@@ -152,9 +179,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     float zt = -INFINITY, acc = 0.f;
     unsigned kt = 0u, idt = 0xFFFFFFFFu;
     bool nan = false;
-    for (int c0 = 0; c0 < V; c0 += kDCH) {
-      const int len = min(kDCH, V - c0);
-      stage<DT>(P, raw, row, c0, len);
+    stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int c0, int len) {
       for (int j = 0; j < kDPer; ++j) {
         const int e = j * kDT + tid;   // consecutive threads, consecutive entries
         if (e >= len) break;
@@ -170,8 +195,8 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
         }
         acc += ex2_approx(__fmul_rn(__fsub_rn(z, zt), kLog2e));
       }
-      __syncthreads();
-    }
+      return true;
+    });
     // block max key, lowest id among its holders, mass rescaled to the block max z
     unsigned kb = __reduce_max_sync(0xFFFFFFFFu, kt);
     if ((tid & 31) == 0) ured[tid >> 5] = kb;
@@ -210,9 +235,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
       for (int b = tid; b < 256 * 16; b += kDT) lpm[b] = 0.f;
     float above = 0.f;
     __syncthreads();
-    for (int c0 = 0; c0 < V; c0 += kDCH) {
-      const int len = min(kDCH, V - c0);
-      stage<DT>(P, raw, row, c0, len);
+    stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int, int len) {
       for (int j = 0; j < kDPer; ++j) {
         const int e = j * kDT + tid;
         if (e >= len) break;
@@ -225,8 +248,8 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
         else if (kh == hb) atomicAdd(&hist[key & 255u], ms);
         else above += ms;
       }
-      __syncthreads();
-    }
+      return true;
+    });
     if (D.pass == 3) {
       const float a = bsum(above, red);
       if (tid == 0) hist[256] = a;
@@ -250,15 +273,13 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
   const uint32_t kdraw = max(tau ? tie_floor<DT, 16>(tau, T) : 0u, zero_mass_cut<DT, 16>(M, T));
   if (D.pass == 4) {
     float k = 0.f;
-    for (int c0 = 0; c0 < V; c0 += kDCH) {
-      const int len = min(kDCH, V - c0);
-      stage<DT>(P, raw, row, c0, len);
+    stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int, int len) {
       for (int j = 0; j < kDPer; ++j) {
         const int e = j * kDT + tid;
         if (e < len && key16(raw[e]) >= kdraw) k += mass_of(Dt::to_f32(raw[e]), T, rT, M);
       }
-      __syncthreads();
-    }
+      return true;
+    });
     const float K = bsum(k, red);
     if (tid == 0) D.gout[i] = K;
     return;
@@ -273,9 +294,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
   }
   float run = 0.f;       // kept mass of the chunks before this one
   int found = -1, lastk = -1;
-  for (int c0 = 0; c0 < V && found < 0; c0 += kDCH) {
-    const int len = min(kDCH, V - c0);
-    stage<DT>(P, raw, row, c0, len);
+  stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int c0, int len) {
     float s = 0.f;
     int lk = -1;
     for (int j = 0; j < kDPer; ++j) {
@@ -324,8 +343,8 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     if (mm != static_cast<unsigned>(INT_MAX) && mm != 0xFFFFFFFFu) found = P.vocab_offset + c0 + static_cast<int>(mm);
     else if (ll > 0u) lastk = P.vocab_offset + c0 + static_cast<int>(ll) - 1;
     run += total;
-    __syncthreads();
-  }
+    return found < 0;
+  });
   if (tid == 0) *out = found >= 0 ? found : lastk;   // rounding: the slice's last kept entry
 }
 
