@@ -180,14 +180,15 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     unsigned kt = 0u, idt = 0xFFFFFFFFu;
     bool nan = false;
     stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int c0, int len) {
+#pragma unroll 4
       for (int j = 0; j < kDPer; ++j) {
         const int e = j * kDT + tid;   // consecutive threads, consecutive entries
-        if (e >= len) break;
+        if (e >= len) continue;
         const uint32_t key = key16(raw[e]);
         const float y = Dt::to_f32(raw[e]);
         if (y != y) { nan = true; continue; }
         if (key > kt) { kt = key; idt = static_cast<unsigned>(P.vocab_offset + c0 + e); }
-        const float z = __fdiv_rn(y, T);
+        const float z = quot_rn(y, T, rT);   // the quotient every mass here uses
         if (z == -INFINITY) continue;   // mass 0
         if (z > zt) {
           acc = (zt == -INFINITY) ? 0.f : __fmul_rn(acc, ex2_approx(__fmul_rn(__fsub_rn(zt, z), kLog2e)));
@@ -236,9 +237,10 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     float above = 0.f;
     __syncthreads();
     stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int, int len) {
+#pragma unroll 4
       for (int j = 0; j < kDPer; ++j) {
         const int e = j * kDT + tid;
-        if (e >= len) break;
+        if (e >= len) continue;
         const uint32_t key = key16(raw[e]);
         const int kh = static_cast<int>(key >> 8);
         if (D.pass == 3 && kh < hb) continue;
