@@ -391,6 +391,20 @@ def run_native(a):
                             "all-gather / all-reduce between them)",
                 "us_per_step": 1e3 * vq["ms_step"], "rows_per_s": vq["value"], "rows_refused": vq["rows_refused"],
                 "scaling": "strong"}
+        else:
+            # the other single-GPU configs: configs[2] (penalised) and
+            # configs[4] (what the sampler adds to a graph-captured decode step)
+            us_rp, us_all, n3, _, _ = c3_measure(a, dev, min(a.steps, 400))
+            extra["c3_penalised"] = {
+                "workload": "configs[2]: B=128 V=151936 fp16, 384-token Zipf histories, T 0.8, top-p 0.95",
+                "us_repetition_only": us_rp, "us_repetition_frequency_presence": us_all, "steps": n3}
+            rows5, n5 = decode_measure(a, dev)
+            extra["c5_decode_added_us"] = {
+                "workload": "configs[4] shapes: LM head 2048 -> 151936 fp16 (random-init weights) in a CUDA graph, "
+                            "with and without SamplingManager.sample + update_penalties (T 0.7, top-p 0.9, "
+                            "repetition penalty 1.1); µs added per step by concurrency",
+                "per_concurrency": {b: round(r["us_added"], 2) for b, r in rows5.items()},
+                "us_head": {b: round(r["us_head"], 2) for b, r in rows5.items()}, "steps": n5}
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -575,6 +589,67 @@ def c4_batch_measure(a, ws, rank, local, dev, steps):
     return ms, b
 
 
+def decode_measure(a, dev, concurrencies=(1, 8, 32, 128)):
+    """What the sampling calls add to a CUDA-graph decode step at configs[4]
+    shapes, per concurrency (see run_decode); returns the per-B rows and the
+    replay count."""
+    from ecahlang_b200.manager import SamplingManager
+    H, V = 2048, 151936
+    g = torch.Generator(device=dev).manual_seed(5)
+    W = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(torch.float16)
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    per_graph = 10
+    reps = max(3, min(50, a.steps // per_graph))
+    rows = {}
+    for B in concurrencies:
+        h = torch.randn(B, H, device=dev, generator=g).to(torch.float16)
+        logits = torch.empty(B, V, device=dev, dtype=torch.float16)
+        # one request per row, each with a penalty slot (history capacity
+        # for the 384 tokens configs[4] generates), parameters through the
+        # bucket buffers
+        mgr = SamplingManager(V, seq_lens=B, dtype=torch.float16, device=dev, history_capacity=512, seed=1)
+        mgr.init_sampling_buffers(B)
+        mgr.init_cuda_graph_buffers([B])
+        reqs = [f"r{i}" for i in range(B)]
+        for r in reqs:
+            mgr.allocate(r)
+        mgr.fill_cuda_graph_sampling_params(B, B, [0.7] * B, [V] * B, [0.9] * B, rep_pens=[1.1] * B,
+                                            batch_ids=reqs)
+
+        def head():
+            torch.matmul(h, W.t(), out=logits)
+
+        def step():
+            head()
+            ids = mgr.sample(logits, bucket_size=B)
+            mgr.update_penalties(ids, bucket_size=B)
+
+        for _ in range(a.warmup):
+            step()
+        torch.cuda.synchronize()
+        side.wait_stream(stream)
+        times = {}
+        for name, fn in (("head", head), ("head+sampler", step)):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                for _ in range(per_graph):
+                    fn()
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times[name] = 1e3 * e0.elapsed_time(e1) / (reps * per_graph)
+            del gr
+        rows[str(B)] = {"us_head": times["head"], "us_head_sampler": times["head+sampler"],
+                        "us_added": times["head+sampler"] - times["head"]}
+    return rows, reps * per_graph
+
+
 def run_decode(a):
     """configs[4] shapes: what the sampler adds to a CUDA-graph decode step.
     Per concurrency B in {1, 8, 32, 128}: graph A = the LM head (fp16 GEMM,
@@ -594,84 +669,23 @@ def run_decode(a):
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    from ecahlang_b200.manager import SamplingManager
-    H, V = 2048, 151936
-    g = torch.Generator(device=dev).manual_seed(5)
-    W = (torch.randn(V, H, device=dev, generator=g) * 0.02).to(torch.float16)
-    stream = torch.cuda.current_stream(dev)
-    side = torch.cuda.Stream(dev)
-    per_graph = 10
-    reps = max(3, min(50, a.steps // per_graph))
-    rows = {}
     with ClockSampler(local) as clk:
-        for B in (1, 8, 32, 128):
-            h = torch.randn(B, H, device=dev, generator=g).to(torch.float16)
-            logits = torch.empty(B, V, device=dev, dtype=torch.float16)
-            # one request per row, each with a penalty slot (history capacity
-            # for the 384 tokens configs[4] generates), parameters through the
-            # bucket buffers
-            mgr = SamplingManager(V, seq_lens=B, dtype=torch.float16, device=dev, history_capacity=512, seed=1)
-            mgr.init_sampling_buffers(B)
-            mgr.init_cuda_graph_buffers([B])
-            reqs = [f"r{i}" for i in range(B)]
-            for r in reqs:
-                mgr.allocate(r)
-            mgr.fill_cuda_graph_sampling_params(B, B, [0.7] * B, [V] * B, [0.9] * B, rep_pens=[1.1] * B,
-                                                batch_ids=reqs)
-
-            def head():
-                torch.matmul(h, W.t(), out=logits)
-
-            def step():
-                head()
-                ids = mgr.sample(logits, bucket_size=B)
-                mgr.update_penalties(ids, bucket_size=B)
-
-            for _ in range(a.warmup):
-                step()
-            torch.cuda.synchronize()
-            side.wait_stream(stream)
-            times = {}
-            for name, fn in (("head", head), ("head+sampler", step)):
-                gr = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gr, stream=side):
-                    for _ in range(per_graph):
-                        fn()
-                gr.replay()
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                for _ in range(reps):
-                    gr.replay()
-                e1.record(stream)
-                torch.cuda.synchronize()
-                times[name] = 1e3 * e0.elapsed_time(e1) / (reps * per_graph)
-                del gr
-            rows[str(B)] = {"us_head": times["head"], "us_head_sampler": times["head+sampler"],
-                            "us_added": times["head+sampler"] - times["head"]}
+        rows, n = decode_measure(a, dev)
     print(json.dumps({
         "metric": "µs the sampler adds to a CUDA-graph decode step (configs[4] shapes: LM head 2048 -> 151936 fp16)",
         "value": rows["128"]["us_added"], "unit": "us", "higher_is_better": False, "n_gpus": 1,
-        "steps": reps * per_graph, "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
+        "steps": n, "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
         "config": {"workload": "c5 decode step: LM head GEMM (+ SamplingManager.sample + update_penalties), "
                                "random-init weights N(0, 0.02^2), T=0.7, top_p=0.9, repetition penalty 1.1 "
-                               "with per-request histories", "launch": f"CUDA-graph replays of {per_graph} steps"},
+                               "with per-request histories", "launch": "CUDA-graph replays of 10 steps"},
         "per_concurrency": rows, "clocks": clk.summary(),
     }), flush=True)
 
 
-def run_c3(a):
-    """configs[2]: B=128, V=151936 fp16, Zipf histories, T 0.8, top-p 0.95.
-    Two figures of one JSON object, both on the row kernel (a wide nucleus,
-    so the dense top-p path): the repetition penalty alone, and repetition +
-    frequency + presence penalties (the penalised logits stay fp16).  CUDA-
-    graph replays over rotating input copies, CUDA events.  One GPU; other
-    ranks exit."""
-    ws, rank, local = _dist()
-    if rank != 0:
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+def c3_measure(a, dev, steps):
+    """configs[2] on one GPU: µs per launch with the repetition penalty alone
+    and with frequency + presence penalties too (CUDA-graph replays over
+    rotating input copies, CUDA events)."""
     from ecahlang_b200 import sampler as S
     from ecahlang_b200 import workloads as W
     w = W.config3(seed=0)
@@ -691,8 +705,8 @@ def run_c3(a):
     out = torch.zeros(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
-    chunk = min(a.steps, 2 * nbuf)
-    reps = max(1, a.steps // chunk)
+    chunk = min(steps, 2 * nbuf)
+    reps = max(1, steps // chunk)
 
     def timed(fn):
         for i in range(a.warmup):
@@ -714,15 +728,31 @@ def run_c3(a):
         del g
         return 1e3 * e0.elapsed_time(e1) / (reps * chunk)
 
+    us_rp = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
+                                     penalty=pen, row_slot=row_slot))
+    us_all = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
+                                      freq_pen=fp, pres_pen=pp, penalty=pen, row_slot=row_slot,
+                                      freq_pres=True))
+    return us_rp, us_all, reps * chunk, chunk, nbuf
+
+
+def run_c3(a):
+    """configs[2]: B=128, V=151936 fp16, Zipf histories, T 0.8, top-p 0.95.
+    Two figures of one JSON object, both on the row kernel (a wide nucleus,
+    so the dense top-p path): the repetition penalty alone, and repetition +
+    frequency + presence penalties (the penalised logits stay fp16).  CUDA-
+    graph replays over rotating input copies, CUDA events.  One GPU; other
+    ranks exit."""
+    ws, rank, local = _dist()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     with ClockSampler(local) as clk:
-        us_rp = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
-                                         penalty=pen, row_slot=row_slot))
-        us_all = timed(lambda i: S.launch(bufs[i % nbuf], T, K, P, out, wsb, uniforms=U, rep_factor=rf,
-                                          freq_pen=fp, pres_pen=pp, penalty=pen, row_slot=row_slot,
-                                          freq_pres=True))
+        us_rp, us_all, n, chunk, nbuf = c3_measure(a, dev, a.steps)
     print(json.dumps({
         "metric": "penalised sampling step (configs[2]: B=128, V=151936 fp16, T 0.8, top-p 0.95)",
-        "value": us_rp, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": reps * chunk,
+        "value": us_rp, "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": n,
         "warmup": a.warmup, "dtype": "f16", "data": "synthetic",
         "config": {"workload": "c3_penalised B=128 V=151936 fp16, 384-token Zipf histories",
                    "launch": f"CUDA-graph replays of {chunk} launches", "l2": f"{nbuf} rotating input copies"},
