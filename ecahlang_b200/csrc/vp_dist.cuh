@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
   using Dt = DType<DT>;
   __shared__ __align__(16) uint16_t rawb[2][kDCH];
   __shared__ float hist[257];
-  // pass 2: per high key byte, 16 lane columns (lanes l and l + 16 share
-  // one), so the lanes of a warp do not pile onto one bin's address
+  // passes 2 and 3: per key byte (high, or low inside the chosen high byte),
+  // 16 lane columns (lanes l and l + 16 share one), so the lanes of a warp do
+  // not pile onto one bin's address
   __shared__ float lpm[256 * 16];
   __shared__ float red[kDT / 32];
   __shared__ unsigned ured[kDT / 32];
@@ -232,8 +233,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
       return;
     }
     for (int b = tid; b < 257; b += kDT) hist[b] = 0.f;
-    if (D.pass == 2)
-      for (int b = tid; b < 256 * 16; b += kDT) lpm[b] = 0.f;
+    for (int b = tid; b < 256 * 16; b += kDT) lpm[b] = 0.f;
     float above = 0.f;
     __syncthreads();
     stream_slice<DT>(P, rawb, row, V, [&](const uint16_t* raw, int, int len) {
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
         const float ms = mass_of(Dt::to_f32(raw[e]), T, rT, M);
         if (!(ms > 0.f)) continue;
         if (D.pass == 2) atomicAdd(&lpm[(kh << 4) | (tid & 15)], ms);
-        else if (kh == hb) atomicAdd(&hist[key & 255u], ms);
+        else if (kh == hb) atomicAdd(&lpm[((key & 255u) << 4) | (tid & 15)], ms);
         else above += ms;
       }
       return true;
@@ -255,14 +255,13 @@ __global__ void __launch_bounds__(kDT) vp_dist_kernel(const __grid_constant__ DP
     if (D.pass == 3) {
       const float a = bsum(above, red);
       if (tid == 0) hist[256] = a;
-    } else {
-      // the lane columns of each bin, in column order
-      for (int b = tid; b < 256; b += kDT) {
-        float t = 0.f;
+    }
+    // the lane columns of each bin, in column order
+    for (int b = tid; b < 256; b += kDT) {
+      float t = 0.f;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) t += lpm[(b << 4) | c];
-        hist[b] = t;
-      }
+      for (int c = 0; c < 16; ++c) t += lpm[(b << 4) | c];
+      hist[b] = t;
     }
     __syncthreads();
     const int width = (D.pass == 2) ? 256 : 257;
