@@ -134,3 +134,30 @@ def test_record_top_p_nucleus_beyond_window():
     orc = run_oracle(x, T, K, P, U)
     nb = compare(x, T, K, P, U, gpu, orc)
     assert nb <= B // 2
+
+
+def test_record_top_p_max_beyond_round_zero():
+    """A dominant token (and a few runners-up) placed after the first 16384
+    entries, far above the first round's max: the records' histogram, kept
+    from round 0's max upward, does not reach the row max, so the finish
+    counts the records again; also rows whose nucleus is that one token."""
+    B, V = B_UNSPLIT, W.V_QWEN
+    x = _c2_like(76, B, V, torch.float32, sigma=1.0, shift=2.0)
+    g = torch.Generator().manual_seed(76)
+    for r in range(B):
+        pos = 20000 + int(torch.randint(0, V - 20000, (1,), generator=g))
+        x[r, pos] = 30.0 + (r % 5)                  # dominant
+        if r % 2:
+            x[r, (pos + 777) % V] = 28.0 + (r % 3)  # a runner-up two units below
+    x = x.half()
+    P = np.array([(0.5, 0.9, 0.99, 0.999)[r % 4] for r in range(B)], np.float32)
+    T = np.array([(1.0, 3.0, 6.0)[r % 3] for r in range(B)], np.float32)
+    K = np.full(B, V, np.int32)
+    U = row_uniforms(76, 0, B)
+    gpu = run_gpu(x, T, K, P, U, probs=True)
+    orc = run_oracle(x, T, K, P, U)
+    nb = compare(x, T, K, P, U, gpu, orc, probs=gpu[2])
+    # at T = 3 and 6 with p = 0.99 / 0.999 the nucleus spans most of the
+    # bulk, so ids within 1e-6 of a CDF step are common (sets and
+    # probabilities are still checked on those rows)
+    assert nb <= B // 4
