@@ -7,7 +7,11 @@
 //
 // During the stream, per row mode (16-bit keys: fp16/bf16 logits):
 //   - every row: per-thread running (max key, first round holding it);
-//   - rows with top-k (k <= kMaxN) or top-p: a candidate buffer in shared
+//   - unsplit rows with top-k: per chunk of 16 entries its top key (records;
+//     lean_finish); unsplit rows with top-p and no top-k: per chunk its two
+//     top keys, counted into a per-key histogram as they stream
+//     (plean_finish); either finishes without re-streaming the row;
+//   - other rows with top-k (k <= kMaxN) or top-p: a candidate buffer in shared
 //     memory holding, in vocab order, every entry whose key is >= a running
 //     floor f.  f starts at the N0-th largest key of the first round (N0 = k
 //     for top-k rows; for top-p-only rows kDenseN scaled to the round's share
@@ -1358,7 +1362,8 @@ constexpr int kStageWords = kStages * kRVecs * 4;
 //      v = kmax - bL.
 //   2. An entry at or above v that is not a record lies in a chunk whose
 //      top2 is at or above v.  Those chunks (listed in vocab order) are
-//      copied from L2 into shared memory, all at once: their entries at or
+//      copied into shared memory, all copies in flight at once (from L2
+//      where the row still is): their entries at or
 //      above v are added to the histogram and their two records taken out,
 //      which leaves exact counts in every bin up to bL (any other chunk's
 //      entries at or above v are its top1 alone).
