@@ -345,7 +345,10 @@ def run_native(a):
                          "traffic": _traffic("c2_mixed"), "algorithmic_bytes_per_launch": alg},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": B * 4, "ms_per_step": ems / ke, "steps": ke,
-                    "api": "SamplingManager.fill_sampling_params + sample (pinned host buffers)"},
+                    "api": "SamplingManager.fill_sampling_params + sample (pinned host buffers)",
+                    "note": ("bound by the host-to-device copy of each rank's logits from pinned host memory "
+                             f"({bytes_in / 1e6:.1f} MB per step and rank); at N > 1 the ranks copy at once and "
+                             "share the host's memory and PCIe bandwidth, so the per-step time grows with N")},
             # one sampler kernel per step; no other kernels run in the timed region
             "gpu_launches": a.steps,
             "clocks": clk.summary(),
